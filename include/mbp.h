@@ -1,0 +1,129 @@
+/*
+ * mbp.h -- C ABI of the B200 (sm_100a) small-M projection library (libmbp.so).
+ *
+ * The library computes out[M, N] = x[M, K] . W[N, K]^T for small token counts M from weights stored in a
+ * lossless 12-bit BF16 format, plus the FP32 router as a BF16 hi/lo pair.  Plain pointers and sizes only: all
+ * pointers are DEVICE pointers unless stated, every call is asynchronous on the given CUDA stream and returns
+ * MBP_OK (0) or a negative status (the reference's convention, submission.py sm_launch S:46<494-552>).
+ *
+ * Each entry point names the reference interface it replaces (reference = NathenFernandes/muse-bf16-proj,
+ * file submission.py, "S:<line>"; "S:46<a-b>" = lines a-b of the CUDA text stored compressed on line 46).
+ */
+#ifndef MBP_H
+#define MBP_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (S:46<494-552>: -1 threads, -2 N%RB, -3 K split, -5 m range, -6 smem, -8 launch,
+ *      -9 cluster, -99 unknown instance, -100 tensor-map encode) ---- */
+#define MBP_OK 0
+#define MBP_ERR_ARG (-1)      /* null pointer or bad enum */
+#define MBP_ERR_SHAPE (-2)    /* n % 16, k % 64, n_out > n, or chunk count >= 32767 */
+#define MBP_ERR_SPLIT (-3)    /* impossible geometry */
+#define MBP_ERR_ALIGN (-4)    /* pointer not 16-byte aligned */
+#define MBP_ERR_M (-5)        /* token count out of range */
+#define MBP_ERR_SMEM (-6)     /* shared memory request above the device limit */
+#define MBP_ERR_LAUNCH (-8)   /* cudaLaunchKernelEx failed (cudaGetLastError is left set) */
+#define MBP_ERR_CLUSTER (-9)  /* cluster shape not schedulable */
+#define MBP_ERR_DEVICE (-10)  /* device is not sm_100 */
+#define MBP_ERR_CAP (-11)     /* caller buffer too small */
+#define MBP_ERR_TMAP (-100)   /* cuTensorMapEncodeTiled failed */
+
+/* device status word codes (written by bounded waits instead of trapping; read with mbp_status) */
+#define MBP_DEV_TIMEOUT_FULL 1   /* consumer gave up waiting for a stage's bytes */
+#define MBP_DEV_TIMEOUT_EMPTY 2  /* producer gave up waiting for a stage to drain */
+#define MBP_DEV_TIMEOUT_MMA 3    /* tensor-core completion did not arrive */
+
+/* ---- weight formats ---- */
+#define MBP_UNIT_ROWS 16
+#define MBP_UNIT_COLS 64
+#define MBP_C12_UNIT_BYTES 1536 /* 1024 weights x 12 bits */
+#define MBP_RAW_UNIT_BYTES 2048 /* 1024 weights x 16 bits */
+
+#define MBP_BASE_MATRIX 0 /* one exponent base per matrix: byte-identical to the reference (S:104-125) */
+#define MBP_BASE_TILE 1   /* one exponent base per 16-row tile */
+
+/* A 12-bit packed matrix W[n, k] in device memory (layout: S:82-125 units, generalised escape list).
+ *   units   [n/16][k/64][1536] bytes, row-tile major
+ *   bases   [n/16]  exponent base (7 high exponent bits) of each 16-row tile
+ *   esc_off [(n/16)*(k/64) + 1] int32: escapes of unit u are esc[esc_off[u] .. esc_off[u+1])
+ *   esc     [n_esc] uint32 entries  chunk << 17 | lane << 12 | value << 7 | xor7  (NULL when n_esc == 0) */
+typedef struct mbp_c12 {
+  const uint8_t* units;
+  const uint8_t* bases;
+  const int32_t* esc_off;
+  const uint32_t* esc;
+  int32_t n;
+  int32_t k;
+  int64_t n_esc;
+} mbp_c12;
+
+/* An FP32 matrix stored as a BF16 hi/lo pair (S:876-879), uncompressed units (S:98-101):
+ *   units [n/16][k/64][2][2048] bytes: the hi unit then the lo unit of each 16x64 block. */
+typedef struct mbp_hilo {
+  const uint8_t* units;
+  int32_t n;
+  int32_t k;
+} mbp_hilo;
+
+/* Launch geometry of the weight-streaming GEMV.  Zero-initialise and call mbp_gemv_plan, or fill by hand. */
+typedef struct mbp_gemv_geom {
+  int32_t rb;      /* 16-row tiles per CTA */
+  int32_t rtw;     /* 16-row tiles per consumer warp (1 or 2) */
+  int32_t split;   /* CTAs splitting K = cluster size (1..16) */
+  int32_t wki;     /* consumer warps splitting a CTA's K range */
+  int32_t kci;     /* 64-column chunks per consumer warp per pipeline stage */
+  int32_t stages;  /* pipeline depth */
+} mbp_gemv_geom;
+
+/* ---- library / device ---- */
+int mbp_version(void);
+/* 0 when `device` is an sm_100 part this library was built for. */
+int mbp_device_check(int device);
+/* Reads (and with clear != 0 resets) the device status word after the stream has been synchronised. */
+int mbp_status(int* status, int clear);
+
+/* ---- GPU packer (replaces the host-side torch packer sm_units/sm_c12_bytes/sm_stream, S:82-227) ----
+ * Two phases, because the escape count is known only after the first:
+ *   1. mbp_pack_c12 writes units, bases and esc_off (esc_off[(n/16)*(k/64)] = total escape count);
+ *   2. after reading that total, the caller allocates esc and calls mbp_pack_c12_escapes.
+ * `workspace` must hold mbp_pack_c12_workspace(n, k) bytes. w is BF16 row-major [n, k], 16-byte aligned. */
+size_t mbp_pack_c12_workspace(int n, int k);
+int mbp_pack_c12(const uint16_t* w, int n, int k, int base_mode, uint8_t* units, uint8_t* bases, int32_t* esc_off,
+                 void* workspace, size_t workspace_bytes, cudaStream_t stream);
+int mbp_pack_c12_escapes(const uint16_t* w, int n, int k, const uint8_t* bases, const int32_t* esc_off,
+                         uint32_t* esc, cudaStream_t stream);
+/* Exact inverse (verification on the device, like the reference's sm_c12_unpack check S:168-170). */
+int mbp_unpack_c12(const mbp_c12* w, uint16_t* w_out, cudaStream_t stream);
+
+/* FP32 [n, k] -> hi/lo units (S:876-879 split + S:98-101 layout). */
+int mbp_pack_hilo(const float* w, int n, int k, uint8_t* units, cudaStream_t stream);
+
+/* ---- weight-streaming GEMV, M <= 32 per token block (replaces sm_launch S:48-53 / S:46<555-561> and its
+ * clones m32_launch S:418-423, the mw launcher S:2398, the smallm2/smtrace/v18 GEMVs) ----
+ * out[m, n_out] = x[m, k] . W[0:n_out, :]^T, FP32 accumulation.  x BF16 row-major [m, k] (16-byte aligned);
+ * out BF16 (mbp_gemv_c12) or FP32 (mbp_gemv_c12_f32) row-major with leading dimension ldo (elements).
+ * n_out <= n, n_out % 16 == 0 (the reference's unpooler uses the first 1024 rows at M <= 8, S:272-273).
+ * m >= 1; m > 32 runs 32-token blocks.  geom may be NULL (planned internally). */
+int mbp_gemv_plan(int n_out, int k, int m, mbp_gemv_geom* geom);
+int mbp_gemv_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo,
+                 const mbp_gemv_geom* geom, cudaStream_t stream);
+int mbp_gemv_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
+                     const mbp_gemv_geom* geom, cudaStream_t stream);
+
+/* ---- FP32 router through the hi/lo pair (replaces rr_launch / rr_scalar / rr_small S:856-861, routertail
+ * S:5424, rwdl S:5377): out_f32[m, n] = x . hi^T + x . lo^T, FP32 accumulation. ---- */
+int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,
+                    cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MBP_H */

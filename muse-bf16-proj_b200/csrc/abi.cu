@@ -1,0 +1,28 @@
+// Library-level entry points: version, device check, and the device status word (one per translation unit).
+#include "common.cuh"
+
+int mbp_status_pack(int* v, int clear);
+int mbp_status_gemv(int* v, int clear);
+
+extern "C" {
+
+int mbp_version(void) { return 1; }
+
+int mbp_device_check(int device) {
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    cudaGetLastError();
+    return MBP_ERR_DEVICE;
+  }
+  return prop.major == 10 && prop.minor == 0 ? MBP_OK : MBP_ERR_DEVICE;
+}
+
+int mbp_status(int* status, int clear) {
+  if (!status) return MBP_ERR_ARG;
+  *status = 0;
+  int rc = mbp_status_pack(status, clear);
+  if (rc == MBP_OK) rc = mbp_status_gemv(status, clear);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,598 @@
+// Weight-streaming GEMV for small token counts: out[m, n] = x[m, k] . W[n, k]^T, FP32 accumulation.
+//
+// Replaces the reference's family of M <= 32 GEMVs (submission.py: sm_gemv S:46<177-477>, m32_gemv S:416,
+// cpstage S:1649/S:1920, smallm2 S:2696, smtrace S:3844, v18d/v18s S:6586/S:6886, router rr_small S:943).
+// Same math (swap-AB mma.sync m16n8k16: 16 weight rows are the A operand decoded in registers, 8 tokens are B),
+// re-designed for B200:
+//
+//   * one CTA = one producer warp + `nwc` consumer warps, CTA tile = rb 16-row tiles x a K range;
+//   * the producer streams the packed weights (row-tile-major units, no per-geometry re-ordering) and the x
+//     rows into a `stages`-deep shared-memory ring with 1-D TMA bulk copies completing on mbarriers, weights
+//     with an L2 evict-first policy;
+//   * consumer warp (wr, wk) owns rtw row tiles and the wk-th slice of the CTA's K range; it decodes each
+//     1536-byte unit in registers (3 prmt per 8 weights), patches escapes through an unbounded per-tile list
+//     (escape.cuh), and issues 4 * MT mma.sync per unit;
+//   * split-K: the wki warp slices reduce through shared memory, the `split` CTAs of a thread-block cluster
+//     through distributed shared memory, each rank reducing and storing 1/split of the tile;
+//   * every wait is bounded and reports through the device status word (no trap).
+//
+// The same kernel serves the FP32 router (S:854, S:941, S:943, S:5377, S:5424) with hi/lo BF16 units: two
+// mma.sync per k-step into one FP32 accumulator.
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <type_traits>
+
+#include "common.cuh"
+#include "escape.cuh"
+
+using namespace mbp;
+
+namespace {
+
+enum { FMT_C12 = 0, FMT_HILO = 1 };
+
+constexpr int kMaxThreads = 512;   // 15 consumer warps + 1 producer: 4 warps per SM sub-partition
+constexpr int kMaxSmem = 227 * 1024;
+constexpr int kMaxConsumerWarps = 15;
+
+struct GemvParams {
+  const uint8_t* units;
+  const uint8_t* bases;
+  const int32_t* esc_off;
+  const uint32_t* esc;
+  const uint16_t* x;
+  void* out;
+  int C;     // 64-column chunks (k / 64)
+  int K;     // k
+  int Rout;  // 16-row tiles computed (n_out / 16)
+  int m;     // tokens
+  int ldo;   // leading dimension of out (elements)
+  int rb, split, wki, kci, stages;
+};
+
+struct Layout {
+  int xp;      // bytes per staged x row (kci chunks + 16 bytes of bank-spreading pad)
+  int wbytes;  // weight bytes per stage
+  int sbytes;  // stage bytes
+  int ring;    // ring bytes (also holds the split-K reduction after the main loop)
+  int xr_off;  // per-warp escape XOR masks
+  int bar_off; // full[stages], empty[stages]
+  int total;
+};
+
+__host__ __device__ inline Layout make_layout(int ub, int mt, int rb, int rtw, int wki, int kci, int stages,
+                                              bool c12) {
+  Layout L;
+  L.xp = kci * 128 + 16;
+  L.wbytes = rb * wki * kci * ub;
+  L.sbytes = L.wbytes + wki * 8 * mt * L.xp;
+  int ring = stages * L.sbytes;
+  const int red = (wki + 1) * rb * mt * 32 * 16;
+  if (red > ring) ring = red;
+  L.ring = (ring + 127) & ~127;
+  L.xr_off = L.ring;
+  L.bar_off = L.xr_off + (c12 ? (rb / rtw) * wki * kXorWarpBytes : 0);
+  L.total = L.bar_off + 2 * stages * 8;
+  return L;
+}
+
+template <int FMT>
+struct Fmt;
+template <>
+struct Fmt<FMT_C12> {
+  static constexpr int UB = MBP_C12_UNIT_BYTES;
+};
+template <>
+struct Fmt<FMT_HILO> {
+  static constexpr int UB = 2 * MBP_RAW_UNIT_BYTES;
+};
+
+MBP_DEV void store_out(uint16_t* o, float v) { *o = __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
+MBP_DEV void store_out(float* o, float v) { *o = v; }
+
+template <int FMT, int MT, int RTW, bool F32OUT>
+__global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__ GemvParams p) {
+  using OutT = typename std::conditional<F32OUT, float, uint16_t>::type;
+  constexpr int UB = Fmt<FMT>::UB;
+  constexpr int TOK = 8 * MT;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rows_w = p.rb / RTW;
+  const int nwc = rows_w * p.wki;
+  const Layout L = make_layout(UB, MT, p.rb, RTW, p.wki, p.kci, p.stages, FMT == FMT_C12);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t full0 = sbase + L.bar_off, empty0 = full0 + 8 * p.stages;
+
+  const int r0 = blockIdx.x * p.rb;
+  const int rvalid = min(p.rb, p.Rout - r0);
+  const int tok0 = blockIdx.z * TOK;
+  const int mtok = min(TOK, p.m - tok0);
+  const int s = blockIdx.y;
+  const int cs = (int)((long long)s * p.C / p.split), ce = (int)((long long)(s + 1) * p.C / p.split);
+  const int Lk = (ce - cs + p.wki - 1) / p.wki;  // chunks per consumer-warp slice
+  const int nit = (Lk + p.kci - 1) / p.kci;
+
+  if (tid == 0) {
+    for (int i = 0; i < p.stages; ++i) {
+      mbar_init(full0 + 8 * i, 1);
+      mbar_init(empty0 + 8 * i, nwc);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  float acc[RTW][MT][4];
+#pragma unroll
+  for (int j = 0; j < RTW; ++j)
+#pragma unroll
+    for (int n = 0; n < MT; ++n)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[j][n][c] = 0.f;
+
+  const int wr = warp % rows_w, wk = warp / rows_w;
+  if (warp == nwc) {
+    // ---------------- producer: one lane per bulk copy ----------------
+    const uint64_t pol = policy_evict_first();
+    for (int it = 0; it < nit; ++it) {
+      const int st = it % p.stages;
+      const uint32_t ph = (uint32_t)(it / p.stages) & 1u;
+      if (it >= p.stages && !mbar_wait(empty0 + 8 * st, ph ^ 1u, MBP_DEV_TIMEOUT_EMPTY)) break;
+      uint32_t bytes = 0;
+      for (int q = 0; q < p.wki; ++q) {
+        const int c0 = cs + q * Lk + it * p.kci, e = min(cs + (q + 1) * Lk, ce);
+        const int nk = max(0, min(p.kci, e - c0));
+        bytes += (uint32_t)nk * (uint32_t)(rvalid * UB + mtok * 128);
+      }
+      const uint32_t stage = sbase + st * L.sbytes, fb = full0 + 8 * st;
+      if (lane == 0) mbar_arrive_expect_tx(fb, bytes);
+      __syncwarp();
+      for (int i = lane; i < rvalid * p.wki; i += 32) {
+        const int rr = i / p.wki, q = i % p.wki;
+        const int c0 = cs + q * Lk + it * p.kci, e = min(cs + (q + 1) * Lk, ce);
+        const int nk = min(p.kci, e - c0);
+        if (nk > 0)
+          bulk_g2s_hint(stage + (uint32_t)((rr * p.wki + q) * p.kci) * UB,
+                        p.units + ((size_t)(r0 + rr) * p.C + c0) * UB, (uint32_t)nk * UB, fb, pol);
+      }
+      for (int i = lane; i < p.wki * mtok; i += 32) {
+        const int q = i / mtok, tk = i % mtok;
+        const int c0 = cs + q * Lk + it * p.kci, e = min(cs + (q + 1) * Lk, ce);
+        const int nk = min(p.kci, e - c0);
+        if (nk > 0)
+          bulk_g2s(stage + L.wbytes + (uint32_t)((q * TOK + tk) * L.xp), p.x + (size_t)(tok0 + tk) * p.K + (size_t)c0 * 64,
+                   (uint32_t)nk * 128, fb);
+      }
+    }
+  } else {
+    // ---------------- consumers ----------------
+    const int b = cs + wk * Lk, e = min(cs + (wk + 1) * Lk, ce);
+    uint32_t T0[RTW], T1[RTW];
+    EscCursor cur[RTW];
+    const uint32_t xr = sbase + L.xr_off + warp * kXorWarpBytes;
+    if constexpr (FMT == FMT_C12) {
+      xor_mask_clear(xr, lane);
+#pragma unroll
+      for (int j = 0; j < RTW; ++j) {
+        const int rt = r0 + wr * RTW + j;
+        T0[j] = T1[j] = 0;
+        if (rt < p.Rout && b < e) {
+          const uint32_t base = p.bases[rt];
+          T0[j] = table_lo(base);
+          T1[j] = table_hi(base);
+          cur[j].init(p.esc, p.esc_off[(size_t)rt * p.C + b], p.esc_off[(size_t)rt * p.C + e], lane);
+        } else {
+          cur[j].init(p.esc, 0, 0, lane);
+        }
+      }
+    }
+    for (int it = 0; it < nit; ++it) {
+      const int st = it % p.stages;
+      const uint32_t ph = (uint32_t)(it / p.stages) & 1u;
+      if (!mbar_wait(full0 + 8 * st, ph, MBP_DEV_TIMEOUT_FULL)) break;
+      const uint32_t stage = sbase + st * L.sbytes;
+      const int c0 = b + it * p.kci;
+      const int nk = max(0, min(p.kci, e - c0));
+      for (int jc = 0; jc < nk; ++jc) {
+        uint32_t bx[MT][8];
+        const uint32_t xa =
+            stage + L.wbytes + (uint32_t)((wk * TOK + (lane >> 2)) * L.xp + jc * 128 + (lane & 3) * 32);
+#pragma unroll
+        for (int n = 0; n < MT; ++n) {
+          const uint4 v0 = lds128(xa + n * 8 * L.xp), v1 = lds128(xa + n * 8 * L.xp + 16);
+          bx[n][0] = v0.x; bx[n][1] = v0.y; bx[n][2] = v0.z; bx[n][3] = v0.w;
+          bx[n][4] = v1.x; bx[n][5] = v1.y; bx[n][6] = v1.z; bx[n][7] = v1.w;
+        }
+#pragma unroll
+        for (int j = 0; j < RTW; ++j) {
+          const int rr = wr * RTW + j;
+          if (rr >= rvalid) continue;
+          const uint32_t ua = stage + (uint32_t)(((rr * p.wki + wk) * p.kci + jc) * UB) + lane * 16;
+          uint32_t A[16];
+          if constexpr (FMT == FMT_C12) {
+            const uint4 p0 = lds128(ua), p1 = lds128(ua + 512), p2 = lds128(ua + 1024);
+            decode_unit(p0, p1, p2, T0[j], T1[j], A);
+            cur[j].apply((uint32_t)(c0 + jc), A, xr, lane);
+#pragma unroll
+            for (int n = 0; n < MT; ++n)
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                mma_bf16_16816(acc[j][n], A[4 * q], A[4 * q + 1], A[4 * q + 2], A[4 * q + 3], bx[n][2 * q],
+                               bx[n][2 * q + 1]);
+          } else {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint4 v = lds128(ua + h * MBP_RAW_UNIT_BYTES + q * 512);
+                A[4 * q] = v.x; A[4 * q + 1] = v.y; A[4 * q + 2] = v.z; A[4 * q + 3] = v.w;
+              }
+#pragma unroll
+              for (int n = 0; n < MT; ++n)
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  mma_bf16_16816(acc[j][n], A[4 * q], A[4 * q + 1], A[4 * q + 2], A[4 * q + 3], bx[n][2 * q],
+                                 bx[n][2 * q + 1]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * st);
+    }
+  }
+
+  // ---------------- split-K reduction ----------------
+  __syncthreads();  // ring is free: every stage has been consumed
+  const int NI = p.rb * MT * 32;
+  float4* red = reinterpret_cast<float4*>(smem);
+  float4* csum = red + (size_t)p.wki * NI;
+  if (warp < nwc) {
+#pragma unroll
+    for (int j = 0; j < RTW; ++j)
+#pragma unroll
+      for (int n = 0; n < MT; ++n)
+        red[(size_t)wk * NI + ((wr * RTW + j) * MT + n) * 32 + lane] =
+            make_float4(acc[j][n][0], acc[j][n][1], acc[j][n][2], acc[j][n][3]);
+  }
+  __syncthreads();
+  OutT* out = reinterpret_cast<OutT*>(p.out);
+  auto emit = [&](int idx, float4 v) {
+    const int ln = idx & 31, rest = idx >> 5, n = rest % MT, rr = rest / MT;
+    if (rr >= rvalid) return;
+    const int row = (r0 + rr) * 16 + (ln >> 2);
+    const int tk = tok0 + n * 8 + 2 * (ln & 3);
+    if (tk < p.m) {
+      store_out(out + (size_t)tk * p.ldo + row, v.x);
+      store_out(out + (size_t)tk * p.ldo + row + 8, v.z);
+    }
+    if (tk + 1 < p.m) {
+      store_out(out + (size_t)(tk + 1) * p.ldo + row, v.y);
+      store_out(out + (size_t)(tk + 1) * p.ldo + row + 8, v.w);
+    }
+  };
+  const int nthr = blockDim.x;
+  if (p.split == 1) {
+    for (int idx = tid; idx < NI; idx += nthr) {
+      float4 v = red[idx];
+      for (int q = 1; q < p.wki; ++q) {
+        const float4 w = red[(size_t)q * NI + idx];
+        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+      }
+      emit(idx, v);
+    }
+  } else {
+    for (int idx = tid; idx < NI; idx += nthr) {
+      float4 v = red[idx];
+      for (int q = 1; q < p.wki; ++q) {
+        const float4 w = red[(size_t)q * NI + idx];
+        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+      }
+      csum[idx] = v;
+    }
+    cluster_sync();
+    const uint32_t rank = cluster_rank();
+    const int per = (NI + p.split - 1) / p.split;
+    const int i0 = (int)rank * per, i1 = min(NI, i0 + per);
+    const uint32_t caddr = smem_u32(csum);
+    for (int idx = i0 + tid; idx < i1; idx += nthr) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < p.split; ++q) {
+        const float4 w = ld_dsmem_f4(mapa(caddr + (uint32_t)idx * 16, (uint32_t)q));
+        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+      }
+      emit(idx, v);
+    }
+    cluster_sync();  // keep this CTA's partials alive until every rank has read them
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------------------------
+using KernelFn = void (*)(GemvParams);
+
+struct Instance {
+  KernelFn fn;
+  int fmt, mt, rtw;
+  bool f32;
+};
+
+template <int FMT, int MT, int RTW, bool F32>
+KernelFn kernel_ptr() {
+  return reinterpret_cast<KernelFn>(&k_gemv<FMT, MT, RTW, F32>);
+}
+
+KernelFn pick(int fmt, int mt, bool f32) {
+  if (fmt == FMT_C12) {
+    if (mt == 1) return f32 ? kernel_ptr<FMT_C12, 1, 1, true>() : kernel_ptr<FMT_C12, 1, 1, false>();
+    if (mt == 2) return f32 ? kernel_ptr<FMT_C12, 2, 1, true>() : kernel_ptr<FMT_C12, 2, 1, false>();
+    return f32 ? kernel_ptr<FMT_C12, 4, 2, true>() : kernel_ptr<FMT_C12, 4, 2, false>();
+  }
+  if (mt == 1) return kernel_ptr<FMT_HILO, 1, 1, true>();
+  if (mt == 2) return kernel_ptr<FMT_HILO, 2, 1, true>();
+  return kernel_ptr<FMT_HILO, 4, 2, true>();
+}
+
+int mt_of(int m) { return m <= 8 ? 1 : m <= 16 ? 2 : 4; }
+int rtw_of(int mt) { return mt == 4 ? 2 : 1; }
+
+// Per-device one-time function attributes (max dynamic shared memory, non-portable cluster sizes).
+std::mutex g_attr_mu;
+std::map<std::pair<int, KernelFn>, bool> g_attr_done;
+
+int ensure_attrs(KernelFn fn) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MBP_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  auto key = std::make_pair(dev, fn);
+  if (g_attr_done.count(key)) return MBP_OK;
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) !=
+      cudaSuccess)
+    return MBP_ERR_SMEM;
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+      cudaSuccess)
+    return MBP_ERR_CLUSTER;
+  g_attr_done[key] = true;
+  return MBP_OK;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+// Co-resident clusters of `split` CTAs for this kernel/config (cached).
+std::mutex g_occ_mu;
+std::map<std::tuple<int, KernelFn, int, int, int>, int> g_occ;
+
+int max_ctas(KernelFn fn, int split, int threads, int smem) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto key = std::make_tuple(dev, fn, split, threads, smem);
+  {
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    auto it = g_occ.find(key);
+    if (it != g_occ.end()) return it->second;
+  }
+  int ctas = 0;
+  if (ensure_attrs(fn) == MBP_OK) {
+    if (split == 1) {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reinterpret_cast<const void*>(fn), threads, smem) ==
+          cudaSuccess)
+        ctas = per_sm * sm_count();
+    } else {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, split, 1);
+      cfg.blockDim = dim3(threads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 1;
+      attr.val.clusterDim.y = split;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(fn), &cfg) == cudaSuccess)
+        ctas = clusters * split;
+    }
+  }
+  cudaGetLastError();
+  std::lock_guard<std::mutex> lk(g_occ_mu);
+  g_occ[key] = ctas;
+  return ctas;
+}
+
+int stages_for(int ub, int mt, int rb, int rtw, int wki, int kci, bool c12) {
+  // ~128 KB of weight bytes in flight per CTA, within the shared-memory limit
+  const Layout one = make_layout(ub, mt, rb, rtw, wki, kci, 1, c12);
+  int st = (128 * 1024 + one.wbytes - 1) / one.wbytes;
+  st = st < 2 ? 2 : st > 8 ? 8 : st;
+  while (st > 2 && make_layout(ub, mt, rb, rtw, wki, kci, st, c12).total > kMaxSmem) --st;
+  return st;
+}
+
+int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g);
+
+std::mutex g_plan_mu;
+std::map<std::tuple<int, int, int, int, int, int, bool>, mbp_gemv_geom> g_plans;
+
+// Planned geometries are cached per (device, format, shape, token tile count, output type).
+int plan_impl(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int mt = mt_of(m);
+  const int zb = (m + 8 * mt - 1) / (8 * mt);
+  const auto key = std::make_tuple(dev, fmt, Rout, C, mt, zb, f32);
+  {
+    std::lock_guard<std::mutex> lk(g_plan_mu);
+    auto it = g_plans.find(key);
+    if (it != g_plans.end()) {
+      *g = it->second;
+      return MBP_OK;
+    }
+  }
+  const int rc = plan_search(fmt, Rout, C, m, f32, g);
+  if (rc == MBP_OK) {
+    std::lock_guard<std::mutex> lk(g_plan_mu);
+    g_plans[key] = *g;
+  }
+  return rc;
+}
+
+int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
+  const int ub = fmt == FMT_C12 ? MBP_C12_UNIT_BYTES : 2 * MBP_RAW_UNIT_BYTES;
+  const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt;
+  const int zb = (m + tok - 1) / tok;
+  const KernelFn fn = pick(fmt, mt, f32);
+  double best = 1e30;
+  mbp_gemv_geom bg = {};
+  const int rb_max = ((Rout + rtw - 1) / rtw) * rtw;
+  for (int rb = rtw; rb <= kMaxConsumerWarps * rtw && rb <= rb_max; rb += rtw) {
+    const int rows_w = rb / rtw;
+    const int nblk = (Rout + rb - 1) / rb;
+    for (int split = 1; split <= 16 && split <= C; ++split) {
+      const int cpc = (C + split - 1) / split;
+      int wki = kMaxConsumerWarps / rows_w;
+      if (wki < 1) wki = 1;
+      if (wki > cpc) wki = cpc;
+      const int kci = 1;
+      const int st = stages_for(ub, mt, rb, rtw, wki, kci, fmt == FMT_C12);
+      const Layout L = make_layout(ub, mt, rb, rtw, wki, kci, st, fmt == FMT_C12);
+      if (L.total > kMaxSmem) continue;
+      const int threads = 32 * (rows_w * wki + 1);
+      const long long G = (long long)nblk * split * zb;
+      const int cap = max_ctas(fn, split, threads, L.total);
+      if (cap <= 0) continue;
+      const long long waves = (G + cap - 1) / cap;
+      // critical path: bytes one CTA streams (weights + x), times waves; small penalty per split level
+      const double per_cta = (double)(rb < Rout ? rb : Rout) * cpc * ub + (double)cpc * tok * 128;
+      const double score = waves * per_cta * (1.0 + 0.01 * split) + (G < cap / 2 ? per_cta * 0.25 : 0.0);
+      if (score < best) {
+        best = score;
+        bg.rb = rb;
+        bg.rtw = rtw;
+        bg.split = split;
+        bg.wki = wki;
+        bg.kci = kci;
+        bg.stages = st;
+      }
+    }
+  }
+  if (best >= 1e30) return MBP_ERR_SPLIT;
+  *g = bg;
+  return MBP_OK;
+}
+
+int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* esc_off, const uint32_t* esc,
+           int C, int K, int n_out, const uint16_t* x, int m, void* out, int ldo, bool f32, const mbp_gemv_geom* geom,
+           cudaStream_t stream) {
+  if (m < 1) return MBP_ERR_M;
+  if (n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
+  if (ldo < n_out) return MBP_ERR_SHAPE;
+  if (((uintptr_t)x & 15u) || ((uintptr_t)units & 15u)) return MBP_ERR_ALIGN;
+  const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt;
+  const int Rout = n_out / 16;
+  mbp_gemv_geom g;
+  if (geom) {
+    g = *geom;
+  } else {
+    const int rc = plan_impl(fmt, Rout, C, m, f32, &g);
+    if (rc) return rc;
+  }
+  if (g.rtw != rtw || g.rb < rtw || g.rb % rtw || g.rb / rtw > kMaxConsumerWarps) return MBP_ERR_SPLIT;
+  if (g.split < 1 || g.split > 16 || g.split > C || g.wki < 1 || g.kci < 1 || g.stages < 1) return MBP_ERR_SPLIT;
+  const int rows_w = g.rb / rtw;
+  if (rows_w * g.wki > kMaxConsumerWarps) return MBP_ERR_SPLIT;
+  const int ub = fmt == FMT_C12 ? MBP_C12_UNIT_BYTES : 2 * MBP_RAW_UNIT_BYTES;
+  const Layout L = make_layout(ub, mt, g.rb, rtw, g.wki, g.kci, g.stages, fmt == FMT_C12);
+  if (L.total > kMaxSmem) return MBP_ERR_SMEM;
+  const KernelFn fn = pick(fmt, mt, f32);
+  int rc = ensure_attrs(fn);
+  if (rc) return rc;
+  GemvParams p;
+  p.units = units;
+  p.bases = bases;
+  p.esc_off = esc_off;
+  p.esc = esc;
+  p.x = x;
+  p.out = out;
+  p.C = C;
+  p.K = K;
+  p.Rout = Rout;
+  p.m = m;
+  p.ldo = ldo;
+  p.rb = g.rb;
+  p.split = g.split;
+  p.wki = g.wki;
+  p.kci = g.kci;
+  p.stages = g.stages;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((Rout + g.rb - 1) / g.rb, g.split, (m + tok - 1) / tok);
+  cfg.blockDim = dim3(32 * (rows_w * g.wki + 1));
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (g.split > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = g.split;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, fn, p) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mbp_gemv_plan(int n_out, int k, int m, mbp_gemv_geom* geom) {
+  if (!geom) return MBP_ERR_ARG;
+  if (n_out <= 0 || n_out % 16 || k <= 0 || k % 64) return MBP_ERR_SHAPE;
+  if (m < 1) return MBP_ERR_M;
+  return plan_impl(FMT_C12, n_out / 16, k / 64, m, false, geom);
+}
+
+int mbp_gemv_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo,
+                 const mbp_gemv_geom* geom, cudaStream_t stream) {
+  if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
+  if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
+  if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n) return MBP_ERR_SHAPE;
+  return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, w->k / 64, w->k, n_out, x, m, out, ldo, false, geom,
+                stream);
+}
+
+int mbp_gemv_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
+                     const mbp_gemv_geom* geom, cudaStream_t stream) {
+  if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
+  if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
+  if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n) return MBP_ERR_SHAPE;
+  return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, w->k / 64, w->k, n_out, x, m, out, ldo, true, geom,
+                stream);
+}
+
+int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,
+                    cudaStream_t stream) {
+  if (!w || !w->units || !x || !out) return MBP_ERR_ARG;
+  if (w->n % 16 || w->k % 64 || w->k / 64 > 32766) return MBP_ERR_SHAPE;
+  mbp_gemv_geom g;
+  if (!geom) {
+    const int rc = plan_impl(FMT_HILO, w->n / 16, w->k / 64, m, true, &g);
+    if (rc) return rc;
+    geom = &g;
+  }
+  return launch(FMT_HILO, w->units, nullptr, nullptr, nullptr, w->k / 64, w->k, w->n, x, m, out, ldo, true, geom,
+                stream);
+}
+
+}  // extern "C"
+
+int mbp_status_gemv(int* v, int clear) { return read_status_here(v, clear); }

@@ -1,0 +1,93 @@
+"""B200-native small-M projection: a drop-in for the reference's ``prepare`` / ``kernel_fn`` API.
+
+Reference (NathenFernandes/muse-bf16-proj, submission.py): types ``Weights`` / ``Config`` / ``Inputs`` (S:21-39),
+``prepare(weights) -> state`` (S:7183) and ``kernel_fn(data, state) -> out`` (S:7189).
+
+* ``prepare`` packs every BF16 layer into the lossless 12-bit format on the GPU and the FP32 router into a BF16
+  hi/lo pair, checks the packing round trip bit for bit on the device, and returns the state.
+* ``kernel_fn`` routes one call to one kernel launch: the weight-streaming GEMV (any M, 32-token blocks) for BF16
+  layers and the hi/lo GEMV for the router, writing a NEW output tensor ``[m, n]`` (BF16, FP32 for the
+  router) like the reference (README.md:36; S:404, S:889).
+
+Unlike the reference there is no fallback: an unsupported call raises instead of dropping to SGLang.
+"""
+from __future__ import annotations
+
+from typing import TypedDict
+
+import torch
+
+from ._lib import MbpError, device_status, lib
+from .ops import (BASE_MATRIX, BASE_TILE, PackedC12, PackedHiLo, gemv, gemv_plan, pack_c12, pack_hilo, router,
+                  unpack_c12)
+
+__all__ = ["Weights", "Config", "Inputs", "prepare", "kernel_fn", "MbpError", "PackedC12", "PackedHiLo", "pack_c12",
+           "unpack_c12", "pack_hilo", "gemv", "gemv_plan", "router", "device_status", "BASE_MATRIX", "BASE_TILE"]
+
+LAYERS = ("qkv_gate", "o", "pooler", "unpooler", "router")
+
+
+class Weights(TypedDict):
+    qkv_gate: torch.Tensor  # bfloat16 [N, K]
+    o: torch.Tensor         # bfloat16 [N, K]
+    pooler: torch.Tensor    # bfloat16 [N, K]
+    unpooler: torch.Tensor  # bfloat16 [N, K]
+    router: torch.Tensor    # float32 [E, K]
+
+
+class Config(TypedDict):
+    m: int
+    n: int
+    k: int
+    layer: str
+
+
+class Inputs(TypedDict):
+    x: torch.Tensor
+    config: Config
+
+
+def prepare(weights: Weights, base_mode: int = BASE_TILE, verify: bool = True) -> dict:
+    """Packs every layer on its device.  ``weights`` may hold any subset of the five layers and any shapes with
+    rows % 16 == 0 and columns % 64 == 0.  BF16 tensors take the 12-bit path, FP32 tensors the hi/lo path."""
+    state: dict = {"layers": {}, "hilo": {}, "k": {}}
+    for name, w in weights.items():
+        if not isinstance(w, torch.Tensor) or not w.is_cuda:
+            raise ValueError(f"layer {name}: expected a CUDA tensor")
+        dev = w.device
+        with torch.cuda.device(dev):
+            if lib().mbp_device_check(dev.index) != 0:
+                raise MbpError(-10, f"layer {name} on {dev}")
+            if w.dtype == torch.float32:
+                state["hilo"][name] = pack_hilo(w)
+            elif w.dtype == torch.bfloat16:
+                p = pack_c12(w, base_mode)
+                if verify and not torch.equal(unpack_c12(p), w):
+                    raise RuntimeError(f"layer {name}: 12-bit packing round trip is not exact")
+                state["layers"][name] = p
+            else:
+                raise ValueError(f"layer {name}: unsupported dtype {w.dtype}")
+            state["k"][name] = w.shape[1]
+    return state
+
+
+def kernel_fn(data: Inputs, state: dict) -> torch.Tensor:
+    """One projection: ``x @ W[:n].T`` (BF16 out) or the router's FP32 logits."""
+    x = data["x"]
+    cfg = data["config"]
+    layer, n = cfg["layer"], int(cfg["n"])
+    if x.dim() != 2 or x.dtype != torch.bfloat16 or not x.is_cuda:
+        raise ValueError("x must be a 2-D bf16 CUDA tensor")
+    if not x.is_contiguous():
+        x = x.contiguous()
+    if layer in state["hilo"]:
+        p = state["hilo"][layer]
+        if n != p.n:
+            raise ValueError(f"router output width {n} != {p.n}")
+        return router(p, x)
+    p = state["layers"].get(layer)
+    if p is None:
+        raise KeyError(f"layer {layer!r} was not prepared")
+    if not 0 < n <= p.n or n % 16:
+        raise ValueError(f"n={n} must be a multiple of 16 in (0, {p.n}]")
+    return gemv(p, x, n_out=n)
