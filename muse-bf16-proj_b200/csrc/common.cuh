@@ -3,6 +3,7 @@
 // Everything here is hand-written inline PTX or plain CUDA C++: mbarriers, 1-D bulk copies (TMA engine, no
 // tensor map), thread-block-cluster distributed shared memory, mma.sync, and the 12-bit weight decode.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -103,6 +104,19 @@ MBP_DEV void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32
       : "memory");
 }
 
+// 2-D tiled TMA load (no multicast) of box {x, y} from a tensor map in kernel-parameter space.
+MBP_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+MBP_DEV void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
 MBP_DEV uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -164,9 +178,10 @@ MBP_DEV float4 ld_dsmem_f4(uint32_t addr) {
 // ------------------------------------------------------------------------------------------------------------
 // tensor core (legacy warp-level path): D += A(16x16 bf16) * B(16x8 bf16), FP32 accumulate
 // ------------------------------------------------------------------------------------------------------------
+// Not volatile: a pure function of its operands, so the scheduler may interleave it with loads of later units.
 MBP_DEV void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                             uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

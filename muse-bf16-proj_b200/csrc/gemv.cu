@@ -5,15 +5,18 @@
 // Same math (swap-AB mma.sync m16n8k16: 16 weight rows are the A operand decoded in registers, 8 tokens are B),
 // re-designed for B200:
 //
-//   * one CTA = one producer warp + `nwc` consumer warps, CTA tile = rb 16-row tiles x a K range;
-//   * the producer streams the packed weights (row-tile-major units, no per-geometry re-ordering) and the x
-//     rows into a `stages`-deep shared-memory ring with 1-D TMA bulk copies completing on mbarriers, weights
-//     with an L2 evict-first policy;
-//   * consumer warp (wr, wk) owns rtw row tiles and the wk-th slice of the CTA's K range; it decodes each
-//     1536-byte unit in registers (3 prmt per 8 weights), patches escapes through an unbounded per-tile list
-//     (escape.cuh), and issues 4 * MT mma.sync per unit;
-//   * split-K: the wki warp slices reduce through shared memory, the `split` CTAs of a thread-block cluster
-//     through distributed shared memory, each rank reducing and storing 1/split of the tile;
+//   * one CTA = one producer warp + `nwc` consumer warps; the CTA tile is rb 16-row tiles x a K range;
+//   * per pipeline stage the producer issues, through the TMA engine, one 1-D bulk copy per row tile of `kci`
+//     consecutive packed units (>= 6 KB each; the packed matrix is row-tile-major, so no per-geometry
+//     re-ordering of the weights is needed) with an L2 evict-first policy, plus one 2-D tensor copy per 64-column
+//     chunk of x (128-byte swizzle, so the fragment loads below are bank-conflict free).  Stages are large
+//     (tens of KB): B200's TMA engine only reaches HBM bandwidth with large slots and copies;
+//   * consumer warp (wr, wk) owns rtw row tiles and the wk-th K slice; per stage it loads its units with plain
+//     shared loads first (instruction-level parallelism across units), decodes each 1536-byte unit in registers
+//     (3 prmt per 8 weights), patches escapes through an unbounded per-tile list (escape.cuh) and issues 4*MT
+//     mma.sync per unit into several independent accumulators;
+//   * split-K: the wki K slices reduce through shared memory, the `split` CTAs of a thread-block cluster through
+//     distributed shared memory, each rank reducing and storing 1/split of the tile;
 //   * every wait is bounded and reports through the device status word (no trap).
 //
 // The same kernel serves the FP32 router (S:854, S:941, S:943, S:5377, S:5424) with hi/lo BF16 units: two
@@ -25,6 +28,7 @@
 
 #include "common.cuh"
 #include "escape.cuh"
+#include "tmap.h"
 
 using namespace mbp;
 
@@ -32,19 +36,18 @@ namespace {
 
 enum { FMT_C12 = 0, FMT_HILO = 1 };
 
-constexpr int kMaxThreads = 512;   // 15 consumer warps + 1 producer: 4 warps per SM sub-partition
+constexpr int kMaxThreads = 384;  // 11 consumer warps + 1 producer (up to 168 registers per thread)
 constexpr int kMaxSmem = 227 * 1024;
-constexpr int kMaxConsumerWarps = 15;
+constexpr int kMaxConsumerWarps = 11;
 
-struct GemvParams {
+struct __align__(64) GemvParams {
+  CUtensorMap xmap;  // x [m, k] bf16, box 64 columns x 8*MT rows, 128-byte swizzle
   const uint8_t* units;
   const uint8_t* bases;
   const int32_t* esc_off;
   const uint32_t* esc;
-  const uint16_t* x;
   void* out;
   int C;     // 64-column chunks (k / 64)
-  int K;     // k
   int Rout;  // 16-row tiles computed (n_out / 16)
   int m;     // tokens
   int ldo;   // leading dimension of out (elements)
@@ -52,21 +55,22 @@ struct GemvParams {
 };
 
 struct Layout {
-  int xp;      // bytes per staged x row (kci chunks + 16 bytes of bank-spreading pad)
-  int wbytes;  // weight bytes per stage
-  int sbytes;  // stage bytes
-  int ring;    // ring bytes (also holds the split-K reduction after the main loop)
-  int xr_off;  // per-warp escape XOR masks
-  int bar_off; // full[stages], empty[stages]
-  int total;
+  int xplane;   // bytes of one staged x chunk: 8*MT rows x 128 bytes
+  int xbytes;   // x bytes per stage
+  int sbytes;   // stage bytes (multiple of 1024)
+  int ring;     // ring bytes (also holds the split-K reduction after the main loop)
+  int xr_off;   // per-warp escape XOR masks
+  int bar_off;  // full[stages], empty[stages]
+  int total;    // bytes from the 1024-aligned base
 };
 
 __host__ __device__ inline Layout make_layout(int ub, int mt, int rb, int rtw, int wki, int kci, int stages,
                                               bool c12) {
   Layout L;
-  L.xp = kci * 128 + 16;
-  L.wbytes = rb * wki * kci * ub;
-  L.sbytes = L.wbytes + wki * 8 * mt * L.xp;
+  L.xplane = 8 * mt * 128;
+  L.xbytes = wki * kci * L.xplane;
+  const int wbytes = rb * wki * kci * ub;
+  L.sbytes = (L.xbytes + wbytes + 1023) & ~1023;
   int ring = stages * L.sbytes;
   const int red = (wki + 1) * rb * mt * 32 * 16;
   if (red > ring) ring = red;
@@ -76,6 +80,15 @@ __host__ __device__ inline Layout make_layout(int ub, int mt, int rb, int rtw, i
   L.total = L.bar_off + 2 * stages * 8;
   return L;
 }
+
+inline int smem_request(const Layout& L) { return L.total + 1024; }  // + alignment slack
+
+// Chunks per unrolled consumer pass and independent accumulators per (row tile, token tile), sized so that a
+// pass's unit loads, B fragments and accumulators fit in 128 registers without spills.
+__host__ __device__ constexpr int kc_for(int fmt, int mt) {
+  return fmt == FMT_C12 ? (mt == 1 ? 4 : mt == 2 ? 2 : 1) : (mt == 1 ? 2 : 1);
+}
+__host__ __device__ constexpr int na_for(int fmt, int mt) { return mt == 4 ? 1 : 2 + 2 * (fmt == FMT_C12 && mt == 1); }
 
 template <int FMT>
 struct Fmt;
@@ -96,21 +109,25 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   using OutT = typename std::conditional<F32OUT, float, uint16_t>::type;
   constexpr int UB = Fmt<FMT>::UB;
   constexpr int TOK = 8 * MT;
-  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int KC = kc_for(FMT, MT);  // chunks per unrolled pass
+  constexpr int NA = na_for(FMT, MT);  // independent accumulators per (row tile, token tile)
+  constexpr int NL = FMT == FMT_C12 ? 3 : 8;         // 16-byte loads per lane per unit
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rows_w = p.rb / RTW;
   const int nwc = rows_w * p.wki;
   const Layout L = make_layout(UB, MT, p.rb, RTW, p.wki, p.kci, p.stages, FMT == FMT_C12);
-  const uint32_t sbase = smem_u32(smem);
+  const uint32_t raw_base = smem_u32(smem_raw);
+  const uint32_t sbase = (raw_base + 1023u) & ~1023u;
+  unsigned char* smem = smem_raw + (sbase - raw_base);
   const uint32_t full0 = sbase + L.bar_off, empty0 = full0 + 8 * p.stages;
 
   const int r0 = blockIdx.x * p.rb;
   const int rvalid = min(p.rb, p.Rout - r0);
   const int tok0 = blockIdx.z * TOK;
-  const int mtok = min(TOK, p.m - tok0);
   const int s = blockIdx.y;
   const int cs = (int)((long long)s * p.C / p.split), ce = (int)((long long)(s + 1) * p.C / p.split);
-  const int Lk = (ce - cs + p.wki - 1) / p.wki;  // chunks per consumer-warp slice
+  const int Lk = (ce - cs + p.wki - 1) / p.wki;  // chunks per K slice
   const int nit = (Lk + p.kci - 1) / p.kci;
 
   if (tid == 0) {
@@ -120,19 +137,22 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
     }
     fence_mbar_init();
   }
+  if (warp == nwc && lane == 0) prefetch_tmap(&p.xmap);
   __syncthreads();
 
-  float acc[RTW][MT][4];
+  float acc[RTW][NA][MT][4];
 #pragma unroll
   for (int j = 0; j < RTW; ++j)
 #pragma unroll
-    for (int n = 0; n < MT; ++n)
+    for (int a = 0; a < NA; ++a)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) acc[j][n][c] = 0.f;
+      for (int n = 0; n < MT; ++n)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[j][a][n][c] = 0.f;
 
   const int wr = warp % rows_w, wk = warp / rows_w;
   if (warp == nwc) {
-    // ---------------- producer: one lane per bulk copy ----------------
+    // ---------------- producer ----------------
     const uint64_t pol = policy_evict_first();
     for (int it = 0; it < nit; ++it) {
       const int st = it % p.stages;
@@ -142,26 +162,23 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
       for (int q = 0; q < p.wki; ++q) {
         const int c0 = cs + q * Lk + it * p.kci, e = min(cs + (q + 1) * Lk, ce);
         const int nk = max(0, min(p.kci, e - c0));
-        bytes += (uint32_t)nk * (uint32_t)(rvalid * UB + mtok * 128);
+        bytes += (uint32_t)nk * (uint32_t)(rvalid * UB + L.xplane);
       }
       const uint32_t stage = sbase + st * L.sbytes, fb = full0 + 8 * st;
       if (lane == 0) mbar_arrive_expect_tx(fb, bytes);
       __syncwarp();
       for (int i = lane; i < rvalid * p.wki; i += 32) {
-        const int rr = i / p.wki, q = i % p.wki;
+        const int rr = i / p.wki, q = i - rr * p.wki;
         const int c0 = cs + q * Lk + it * p.kci, e = min(cs + (q + 1) * Lk, ce);
         const int nk = min(p.kci, e - c0);
         if (nk > 0)
-          bulk_g2s_hint(stage + (uint32_t)((rr * p.wki + q) * p.kci) * UB,
+          bulk_g2s_hint(stage + L.xbytes + (uint32_t)((rr * p.wki + q) * p.kci) * UB,
                         p.units + ((size_t)(r0 + rr) * p.C + c0) * UB, (uint32_t)nk * UB, fb, pol);
       }
-      for (int i = lane; i < p.wki * mtok; i += 32) {
-        const int q = i / mtok, tk = i % mtok;
+      for (int i = lane; i < p.wki * p.kci; i += 32) {
+        const int q = i / p.kci, jc = i - q * p.kci;
         const int c0 = cs + q * Lk + it * p.kci, e = min(cs + (q + 1) * Lk, ce);
-        const int nk = min(p.kci, e - c0);
-        if (nk > 0)
-          bulk_g2s(stage + L.wbytes + (uint32_t)((q * TOK + tk) * L.xp), p.x + (size_t)(tok0 + tk) * p.K + (size_t)c0 * 64,
-                   (uint32_t)nk * 128, fb);
+        if (c0 + jc < e) tma_load_2d(stage + (uint32_t)(i * L.xplane), &p.xmap, (c0 + jc) * 64, tok0, fb);
       }
     }
   } else {
@@ -186,56 +203,93 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
         }
       }
     }
-    for (int it = 0; it < nit; ++it) {
-      const int st = it % p.stages;
-      const uint32_t ph = (uint32_t)(it / p.stages) & 1u;
-      if (!mbar_wait(full0 + 8 * st, ph, MBP_DEV_TIMEOUT_FULL)) break;
-      const uint32_t stage = sbase + st * L.sbytes;
-      const int c0 = b + it * p.kci;
-      const int nk = max(0, min(p.kci, e - c0));
-      for (int jc = 0; jc < nk; ++jc) {
+    const int g = lane >> 2, t = lane & 3;
+    // byte offsets inside a stage, fixed for this warp
+    uint32_t uoff[RTW];
+#pragma unroll
+    for (int j = 0; j < RTW; ++j)
+      uoff[j] = (uint32_t)L.xbytes + (uint32_t)((min(wr * RTW + j, p.rb - 1) * p.wki + wk) * p.kci) * UB + lane * 16;
+    const uint32_t xoff = (uint32_t)(wk * p.kci * L.xplane + g * 128);
+    const uint32_t swz0 = ((2 * t) ^ g) << 4, swz1 = ((2 * t + 1) ^ g) << 4;
+    bool rvalid_j[RTW];
+#pragma unroll
+    for (int j = 0; j < RTW; ++j) rvalid_j[j] = wr * RTW + j < rvalid;
+
+    // One pass of KC chunks.  ESC selects the variant that patches escapes; a stage whose chunk range holds
+    // none of this warp's escapes runs the variant without any escape code.
+    auto pass_fn = [&](const unsigned char* stage, int c0, int cl0, int nk, auto esc_tag) {
+      constexpr bool ESC = decltype(esc_tag)::value;
+      uint4 u[KC][RTW][NL];  // all units of the pass first: independent shared loads in flight together
+#pragma unroll
+      for (int jc = 0; jc < KC; ++jc)
+#pragma unroll
+        for (int j = 0; j < RTW; ++j) {
+          const uint4* src = reinterpret_cast<const uint4*>(stage + uoff[j] + (cl0 + jc) * UB);
+#pragma unroll
+          for (int l = 0; l < NL; ++l) u[jc][j][l] = src[l * 32];
+        }
+#pragma unroll
+      for (int jc = 0; jc < KC; ++jc) {
+        const int cl = cl0 + jc;  // chunk within the stage
+        if (cl >= nk) break;
+        const unsigned char* xrow = stage + xoff + cl * L.xplane;
         uint32_t bx[MT][8];
-        const uint32_t xa =
-            stage + L.wbytes + (uint32_t)((wk * TOK + (lane >> 2)) * L.xp + jc * 128 + (lane & 3) * 32);
 #pragma unroll
         for (int n = 0; n < MT; ++n) {
-          const uint4 v0 = lds128(xa + n * 8 * L.xp), v1 = lds128(xa + n * 8 * L.xp + 16);
+          const uint4 v0 = *reinterpret_cast<const uint4*>(xrow + n * 1024 + swz0);
+          const uint4 v1 = *reinterpret_cast<const uint4*>(xrow + n * 1024 + swz1);
           bx[n][0] = v0.x; bx[n][1] = v0.y; bx[n][2] = v0.z; bx[n][3] = v0.w;
           bx[n][4] = v1.x; bx[n][5] = v1.y; bx[n][6] = v1.z; bx[n][7] = v1.w;
         }
 #pragma unroll
         for (int j = 0; j < RTW; ++j) {
-          const int rr = wr * RTW + j;
-          if (rr >= rvalid) continue;
-          const uint32_t ua = stage + (uint32_t)(((rr * p.wki + wk) * p.kci + jc) * UB) + lane * 16;
+          if (!rvalid_j[j]) continue;
           uint32_t A[16];
           if constexpr (FMT == FMT_C12) {
-            const uint4 p0 = lds128(ua), p1 = lds128(ua + 512), p2 = lds128(ua + 1024);
-            decode_unit(p0, p1, p2, T0[j], T1[j], A);
-            cur[j].apply((uint32_t)(c0 + jc), A, xr, lane);
+            decode_unit(u[jc][j][0], u[jc][j][1], u[jc][j][2], T0[j], T1[j], A);
+            if constexpr (ESC) cur[j].apply((uint32_t)(c0 + cl), A, xr, lane);
 #pragma unroll
             for (int n = 0; n < MT; ++n)
 #pragma unroll
               for (int q = 0; q < 4; ++q)
-                mma_bf16_16816(acc[j][n], A[4 * q], A[4 * q + 1], A[4 * q + 2], A[4 * q + 3], bx[n][2 * q],
-                               bx[n][2 * q + 1]);
+                mma_bf16_16816(acc[j][(jc * 4 + q) % NA][n], A[4 * q], A[4 * q + 1], A[4 * q + 2], A[4 * q + 3],
+                               bx[n][2 * q], bx[n][2 * q + 1]);
           } else {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+              for (int h = 0; h < 2; ++h) {
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const uint4 v = lds128(ua + h * MBP_RAW_UNIT_BYTES + q * 512);
-                A[4 * q] = v.x; A[4 * q + 1] = v.y; A[4 * q + 2] = v.z; A[4 * q + 3] = v.w;
+                for (int q = 0; q < 4; ++q) {
+                  const uint4 v = u[jc][j][4 * h + q];
+                  A[4 * q] = v.x; A[4 * q + 1] = v.y; A[4 * q + 2] = v.z; A[4 * q + 3] = v.w;
+                }
+#pragma unroll
+                for (int n = 0; n < MT; ++n)
+#pragma unroll
+                  for (int q = 0; q < 4; ++q)
+                    mma_bf16_16816(acc[j][(jc * 4 + q) % NA][n], A[4 * q], A[4 * q + 1], A[4 * q + 2],
+                                   A[4 * q + 3], bx[n][2 * q], bx[n][2 * q + 1]);
               }
-#pragma unroll
-              for (int n = 0; n < MT; ++n)
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-                  mma_bf16_16816(acc[j][n], A[4 * q], A[4 * q + 1], A[4 * q + 2], A[4 * q + 3], bx[n][2 * q],
-                                 bx[n][2 * q + 1]);
             }
           }
         }
+    };
+
+    for (int it = 0; it < nit; ++it) {
+      const int st = it % p.stages;
+      const uint32_t ph = (uint32_t)(it / p.stages) & 1u;
+      if (!mbar_wait(full0 + 8 * st, ph, MBP_DEV_TIMEOUT_FULL)) break;
+      const unsigned char* stage = smem + st * L.sbytes;
+      const int c0 = b + it * p.kci;
+      const int nk = max(0, min(p.kci, e - c0));
+      bool esc_here = false;
+      if constexpr (FMT == FMT_C12) {
+#pragma unroll
+        for (int j = 0; j < RTW; ++j) esc_here |= (int)cur[j].next_chunk < c0 + nk;
+      }
+      if (esc_here) {
+        for (int cl0 = 0; cl0 < nk; cl0 += KC) pass_fn(stage, c0, cl0, nk, std::true_type{});
+      } else {
+        for (int cl0 = 0; cl0 < nk; cl0 += KC) pass_fn(stage, c0, cl0, nk, std::false_type{});
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * st);
@@ -251,9 +305,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
 #pragma unroll
     for (int j = 0; j < RTW; ++j)
 #pragma unroll
-      for (int n = 0; n < MT; ++n)
-        red[(size_t)wk * NI + ((wr * RTW + j) * MT + n) * 32 + lane] =
-            make_float4(acc[j][n][0], acc[j][n][1], acc[j][n][2], acc[j][n][3]);
+      for (int n = 0; n < MT; ++n) {
+        float4 v = make_float4(acc[j][0][n][0], acc[j][0][n][1], acc[j][0][n][2], acc[j][0][n][3]);
+#pragma unroll
+        for (int a = 1; a < NA; ++a) {
+          v.x += acc[j][a][n][0];
+          v.y += acc[j][a][n][1];
+          v.z += acc[j][a][n][2];
+          v.w += acc[j][a][n][3];
+        }
+        red[(size_t)wk * NI + ((wr * RTW + j) * MT + n) * 32 + lane] = v;
+      }
   }
   __syncthreads();
   OutT* out = reinterpret_cast<OutT*>(p.out);
@@ -272,24 +334,18 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
     }
   };
   const int nthr = blockDim.x;
-  if (p.split == 1) {
-    for (int idx = tid; idx < NI; idx += nthr) {
-      float4 v = red[idx];
-      for (int q = 1; q < p.wki; ++q) {
-        const float4 w = red[(size_t)q * NI + idx];
-        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
-      }
+  for (int idx = tid; idx < NI; idx += nthr) {
+    float4 v = red[idx];
+    for (int q = 1; q < p.wki; ++q) {
+      const float4 w = red[(size_t)q * NI + idx];
+      v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+    }
+    if (p.split == 1)
       emit(idx, v);
-    }
-  } else {
-    for (int idx = tid; idx < NI; idx += nthr) {
-      float4 v = red[idx];
-      for (int q = 1; q < p.wki; ++q) {
-        const float4 w = red[(size_t)q * NI + idx];
-        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
-      }
+    else
       csum[idx] = v;
-    }
+  }
+  if (p.split > 1) {
     cluster_sync();
     const uint32_t rank = cluster_rank();
     const int per = (NI + p.split - 1) / p.split;
@@ -312,12 +368,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
 // ------------------------------------------------------------------------------------------------------------
 using KernelFn = void (*)(GemvParams);
 
-struct Instance {
-  KernelFn fn;
-  int fmt, mt, rtw;
-  bool f32;
-};
-
 template <int FMT, int MT, int RTW, bool F32>
 KernelFn kernel_ptr() {
   return reinterpret_cast<KernelFn>(&k_gemv<FMT, MT, RTW, F32>);
@@ -336,6 +386,7 @@ KernelFn pick(int fmt, int mt, bool f32) {
 
 int mt_of(int m) { return m <= 8 ? 1 : m <= 16 ? 2 : 4; }
 int rtw_of(int mt) { return mt == 4 ? 2 : 1; }
+int ub_of(int fmt) { return fmt == FMT_C12 ? MBP_C12_UNIT_BYTES : 2 * MBP_RAW_UNIT_BYTES; }
 
 // Per-device one-time function attributes (max dynamic shared memory, non-portable cluster sizes).
 std::mutex g_attr_mu;
@@ -364,7 +415,7 @@ int sm_count() {
   return n;
 }
 
-// Co-resident clusters of `split` CTAs for this kernel/config (cached).
+// Co-resident CTAs (clusters of `split` CTAs) for this kernel/config, cached.
 std::mutex g_occ_mu;
 std::map<std::tuple<int, KernelFn, int, int, int>, int> g_occ;
 
@@ -407,16 +458,75 @@ int max_ctas(KernelFn fn, int split, int threads, int smem) {
   return ctas;
 }
 
-int stages_for(int ub, int mt, int rb, int rtw, int wki, int kci, bool c12) {
-  // ~128 KB of weight bytes in flight per CTA, within the shared-memory limit
-  const Layout one = make_layout(ub, mt, rb, rtw, wki, kci, 1, c12);
-  int st = (128 * 1024 + one.wbytes - 1) / one.wbytes;
-  st = st < 2 ? 2 : st > 8 ? 8 : st;
-  while (st > 2 && make_layout(ub, mt, rb, rtw, wki, kci, st, c12).total > kMaxSmem) --st;
-  return st;
+// Geometry search over a bandwidth model fit to measurements on B200:
+//   * the device streams at most ~6.0 TB/s and one SM at most ~45 GB/s, so a launch takes at least
+//     max(all bytes / 6.0 TB/s, bytes of the busiest SM / 45 GB/s);
+//   * the TMA engine only reaches that with stages of ~48-96 KB made of copies of >= 6 KB (kci units per row
+//     tile), 2-4 stages deep;
+//   * each level of cluster split-K costs a fixed reduction / synchronisation overhead;
+//   * ~8 consumer warps per SM (fewer, fatter CTAs when the token tile is large and 2 CTAs fit an SM).
+// Only single-wave launches are considered.
+int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
+  constexpr double kHbmBw = 6.0e12, kSmBw = 45.0e9, kSplitCost = 1.2e-6;
+  const int ub = ub_of(fmt);
+  const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt, kc = kc_for(fmt, mt);
+  const int zb = (m + tok - 1) / tok;
+  const KernelFn fn = pick(fmt, mt, f32);
+  const int sms = sm_count();
+  const double total = (double)Rout * C * ub * zb;
+  double best = 1e30;
+  mbp_gemv_geom bg = {};
+  const int rb_max = ((Rout + rtw - 1) / rtw) * rtw;
+  for (int split = 1; split <= 16 && split <= C; ++split) {
+    const int cpc = (C + split - 1) / split;
+    for (int rb = rtw; rb <= kMaxConsumerWarps * rtw && rb <= rb_max; rb += rtw) {
+      const int rows_w = rb / rtw;
+      const int nblk = (Rout + rb - 1) / rb;
+      const long long G = (long long)nblk * split * zb;
+      // consumer warps: ~8 per CTA, never more than the slice count
+      int wki = (8 + rows_w / 2) / rows_w;
+      if (wki < 1) wki = 1;
+      while (rows_w * wki > kMaxConsumerWarps) --wki;
+      if (wki > cpc) wki = cpc;
+      const int per_slice = (cpc + wki - 1) / wki;
+      // largest copy whose stage stays <= 96 KB; 3-4 stages when they fit
+      int kci = kc;
+      while (kci + kc <= 16 && kci < per_slice && rb * wki * (kci + kc) * ub <= 96 * 1024) kci += kc;
+      const int slot_w = rb * wki * kci * ub;
+      int st = 2;
+      while (st < 4 && (st + 1) * slot_w <= 192 * 1024 &&
+             smem_request(make_layout(ub, mt, rb, rtw, wki, kci, st + 1, fmt == FMT_C12)) <= kMaxSmem)
+        ++st;
+      const Layout L = make_layout(ub, mt, rb, rtw, wki, kci, st, fmt == FMT_C12);
+      if (smem_request(L) > kMaxSmem) continue;
+      const int threads = 32 * (rows_w * wki + 1);
+      const int cap = max_ctas(fn, split, threads, smem_request(L));
+      if (cap <= 0) continue;
+      const long long waves = (G + cap - 1) / cap;
+      const double per_cta = (double)(rb < Rout ? rb : Rout) * cpc * ub + (double)cpc * tok * 128;
+      const long long per_sm = (G + sms - 1) / sms;
+      double t = total / kHbmBw;
+      const double t_sm = per_cta * per_sm / kSmBw;
+      if (t_sm > t) t = t_sm;
+      if (waves > 1) t *= 1.0 + 0.15 * (waves - 1);  // wave tails
+      if (split > 1) t += kSplitCost * (1.0 + 0.1 * split);
+      if (kci * ub < 6144 && kci < per_slice) t *= 1.3;  // small copies starve the TMA engine
+      if (st * slot_w < 96 * 1024) t *= 1.0 + (96.0 * 1024 - st * slot_w) / (192.0 * 1024);
+      if (t < best) {
+        best = t;
+        bg.rb = rb;
+        bg.rtw = rtw;
+        bg.split = split;
+        bg.wki = wki;
+        bg.kci = kci;
+        bg.stages = st;
+      }
+    }
+  }
+  if (best >= 1e30) return MBP_ERR_SPLIT;
+  *g = bg;
+  return MBP_OK;
 }
-
-int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g);
 
 std::mutex g_plan_mu;
 std::map<std::tuple<int, int, int, int, int, int, bool>, mbp_gemv_geom> g_plans;
@@ -444,50 +554,6 @@ int plan_impl(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
   return rc;
 }
 
-int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
-  const int ub = fmt == FMT_C12 ? MBP_C12_UNIT_BYTES : 2 * MBP_RAW_UNIT_BYTES;
-  const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt;
-  const int zb = (m + tok - 1) / tok;
-  const KernelFn fn = pick(fmt, mt, f32);
-  double best = 1e30;
-  mbp_gemv_geom bg = {};
-  const int rb_max = ((Rout + rtw - 1) / rtw) * rtw;
-  for (int rb = rtw; rb <= kMaxConsumerWarps * rtw && rb <= rb_max; rb += rtw) {
-    const int rows_w = rb / rtw;
-    const int nblk = (Rout + rb - 1) / rb;
-    for (int split = 1; split <= 16 && split <= C; ++split) {
-      const int cpc = (C + split - 1) / split;
-      int wki = kMaxConsumerWarps / rows_w;
-      if (wki < 1) wki = 1;
-      if (wki > cpc) wki = cpc;
-      const int kci = 1;
-      const int st = stages_for(ub, mt, rb, rtw, wki, kci, fmt == FMT_C12);
-      const Layout L = make_layout(ub, mt, rb, rtw, wki, kci, st, fmt == FMT_C12);
-      if (L.total > kMaxSmem) continue;
-      const int threads = 32 * (rows_w * wki + 1);
-      const long long G = (long long)nblk * split * zb;
-      const int cap = max_ctas(fn, split, threads, L.total);
-      if (cap <= 0) continue;
-      const long long waves = (G + cap - 1) / cap;
-      // critical path: bytes one CTA streams (weights + x), times waves; small penalty per split level
-      const double per_cta = (double)(rb < Rout ? rb : Rout) * cpc * ub + (double)cpc * tok * 128;
-      const double score = waves * per_cta * (1.0 + 0.01 * split) + (G < cap / 2 ? per_cta * 0.25 : 0.0);
-      if (score < best) {
-        best = score;
-        bg.rb = rb;
-        bg.rtw = rtw;
-        bg.split = split;
-        bg.wki = wki;
-        bg.kci = kci;
-        bg.stages = st;
-      }
-    }
-  }
-  if (best >= 1e30) return MBP_ERR_SPLIT;
-  *g = bg;
-  return MBP_OK;
-}
-
 int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* esc_off, const uint32_t* esc,
            int C, int K, int n_out, const uint16_t* x, int m, void* out, int ldo, bool f32, const mbp_gemv_geom* geom,
            cudaStream_t stream) {
@@ -495,7 +561,7 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   if (n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
   if (ldo < n_out) return MBP_ERR_SHAPE;
   if (((uintptr_t)x & 15u) || ((uintptr_t)units & 15u)) return MBP_ERR_ALIGN;
-  const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt;
+  const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt, kc = kc_for(fmt, mt);
   const int Rout = n_out / 16;
   mbp_gemv_geom g;
   if (geom) {
@@ -505,24 +571,26 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
     if (rc) return rc;
   }
   if (g.rtw != rtw || g.rb < rtw || g.rb % rtw || g.rb / rtw > kMaxConsumerWarps) return MBP_ERR_SPLIT;
-  if (g.split < 1 || g.split > 16 || g.split > C || g.wki < 1 || g.kci < 1 || g.stages < 1) return MBP_ERR_SPLIT;
+  if (g.split < 1 || g.split > 16 || g.split > C || g.wki < 1 || g.kci < kc || g.kci % kc || g.stages < 1)
+    return MBP_ERR_SPLIT;
   const int rows_w = g.rb / rtw;
   if (rows_w * g.wki > kMaxConsumerWarps) return MBP_ERR_SPLIT;
-  const int ub = fmt == FMT_C12 ? MBP_C12_UNIT_BYTES : 2 * MBP_RAW_UNIT_BYTES;
+  const int ub = ub_of(fmt);
   const Layout L = make_layout(ub, mt, g.rb, rtw, g.wki, g.kci, g.stages, fmt == FMT_C12);
-  if (L.total > kMaxSmem) return MBP_ERR_SMEM;
+  if (smem_request(L) > kMaxSmem) return MBP_ERR_SMEM;
   const KernelFn fn = pick(fmt, mt, f32);
   int rc = ensure_attrs(fn);
   if (rc) return rc;
   GemvParams p;
+  if (!encode_bf16_2d(&p.xmap, x, (uint64_t)m, (uint64_t)K, (uint64_t)K, (uint32_t)tok, 64u,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+    return MBP_ERR_TMAP;
   p.units = units;
   p.bases = bases;
   p.esc_off = esc_off;
   p.esc = esc;
-  p.x = x;
   p.out = out;
   p.C = C;
-  p.K = K;
   p.Rout = Rout;
   p.m = m;
   p.ldo = ldo;
@@ -534,7 +602,7 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((Rout + g.rb - 1) / g.rb, g.split, (m + tok - 1) / tok);
   cfg.blockDim = dim3(32 * (rows_w * g.wki + 1));
-  cfg.dynamicSmemBytes = L.total;
+  cfg.dynamicSmemBytes = smem_request(L);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   int na = 0;
@@ -583,6 +651,7 @@ int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int
                     cudaStream_t stream) {
   if (!w || !w->units || !x || !out) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766) return MBP_ERR_SHAPE;
+  if (m < 1) return MBP_ERR_M;
   mbp_gemv_geom g;
   if (!geom) {
     const int rc = plan_impl(FMT_HILO, w->n / 16, w->k / 64, m, true, &g);
