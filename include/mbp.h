@@ -34,6 +34,7 @@ extern "C" {
 #define MBP_ERR_DEVICE (-10)  /* device is not sm_100 */
 #define MBP_ERR_CAP (-11)     /* caller buffer too small */
 #define MBP_ERR_TMAP (-100)   /* cuTensorMapEncodeTiled failed */
+#define MBP_ERR_SCRATCH_LIMIT (-12) /* matrix too tall for the fixed scratch of mbp_pack_c12_noalloc */
 
 /* device status word codes (written by bounded waits instead of trapping; read with mbp_status) */
 #define MBP_DEV_TIMEOUT_FULL 1   /* consumer gave up waiting for a stage's bytes */
@@ -97,6 +98,17 @@ int mbp_status(int* status, int clear);
 size_t mbp_pack_c12_workspace(int n, int k);
 int mbp_pack_c12(const uint16_t* w, int n, int k, int base_mode, uint8_t* units, uint8_t* bases, int32_t* esc_off,
                  void* workspace, size_t workspace_bytes, cudaStream_t stream);
+/* Allocation-free phase 1 of the packer.  No counterpart in the reference.  For callers that cannot allocate
+ * device memory themselves: a loader handed only preallocated weight and output buffers by a host framework
+ * that owns all device memory, or a caller that must not trigger cudaMalloc's implicit device-wide
+ * synchronisation while other streams run.  Same arguments and results as mbp_pack_c12 minus the workspace:
+ * the per-tile histograms live in a fixed 512 KiB device array inside the library (held by every GPU that
+ * loads the library until the process exits), which limits n to 16384 rows (MBP_ERR_SCRATCH_LIMIT beyond).
+ * Calls no cudaMalloc/cudaFree.  Its first call on a device looks up the array's device address, so make that
+ * first call before any stream capture.  All calls share the array: calls that overlap on the GPU (other
+ * streams, other threads) race on it; serialise them. */
+int mbp_pack_c12_noalloc(const uint16_t* w, int n, int k, int base_mode, uint8_t* units, uint8_t* bases,
+                         int32_t* esc_off, cudaStream_t stream);
 int mbp_pack_c12_escapes(const uint16_t* w, int n, int k, const uint8_t* bases, const int32_t* esc_off,
                          uint32_t* esc, cudaStream_t stream);
 /* Exact inverse (verification on the device, like the reference's sm_c12_unpack check S:168-170). */

@@ -10,6 +10,8 @@
 //   k_scan     exclusive scan of per-unit escape counts -> esc_off                              (new: CSR)
 // mbp_pack_c12_escapes:
 //   k_escapes  one warp per unit: entries chunk<<17 | lane<<12 | value<<7 | xor7 in (lane, value) order
+#include <mutex>
+
 #include "common.cuh"
 #include "escape.cuh"
 
@@ -375,3 +377,62 @@ int mbp_pack_hilo(const float* w, int n, int k, uint8_t* units, cudaStream_t str
 }  // extern "C"
 
 int mbp_status_pack(int* v, int clear) { return read_status_here(v, clear); }
+
+// ------------------------------------------------------------------------------------------------------------
+// Allocation-free packer.  Its scratch -- one 128-bin exponent histogram per 16-row tile -- is this fixed
+// device array instead of a caller-provided workspace.  k_hist overwrites every entry it later reads, so
+// nothing has to be cleared between calls; concurrent calls on one device would race on it.
+// ------------------------------------------------------------------------------------------------------------
+namespace {
+constexpr int kNoAllocMaxTiles = 1024;  // n <= 16384 rows: 1024 tiles x 128 bins x 4 bytes = 512 KiB
+constexpr int kMaxDevices = 64;
+}  // namespace
+
+static __device__ __align__(256) int g_pack_scratch[kNoAllocMaxTiles * 128];
+
+namespace {
+std::mutex g_scratch_mu;
+int* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_pack_scratch on the current device, looked up once per device.  In host code the
+// array's name is only a host-side stand-in, so kernels must be given this address.
+int scratch_on_current_device(int** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MBP_ERR_LAUNCH;
+  if (dev < 0 || dev >= kMaxDevices) return MBP_ERR_DEVICE;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_pack_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();
+      return MBP_ERR_LAUNCH;
+    }
+    g_scratch_addr[dev] = static_cast<int*>(p);
+  }
+  *out = g_scratch_addr[dev];
+  return MBP_OK;
+}
+}  // namespace
+
+extern "C" int mbp_pack_c12_noalloc(const uint16_t* w, int n, int k, int base_mode, uint8_t* units,
+                                    uint8_t* bases, int32_t* esc_off, cudaStream_t stream) {
+  if (!w || !units || !bases || !esc_off) return MBP_ERR_ARG;
+  if (base_mode != MBP_BASE_MATRIX && base_mode != MBP_BASE_TILE) return MBP_ERR_ARG;
+  if (!shape_ok(n, k)) return MBP_ERR_SHAPE;
+  if (n / 16 > kNoAllocMaxTiles) return MBP_ERR_SCRATCH_LIMIT;
+  if (!aligned16(w) || !aligned16(units)) return MBP_ERR_ALIGN;
+  int* hist = nullptr;
+  const int rc = scratch_on_current_device(&hist);
+  if (rc != MBP_OK) return rc;
+  const int R = n / 16, C = k / 64;
+  const long long NU = (long long)R * C;
+  k_hist<<<R, 256, 0, stream>>>(w, k, hist);
+  if (base_mode == MBP_BASE_TILE)
+    k_bases<<<R, 128, 0, stream>>>(hist, R, 1, bases);
+  else
+    k_bases<<<1, 128, 0, stream>>>(hist, R, 0, bases);
+  const unsigned blocks = (unsigned)((NU + kWarpsPerCta - 1) / kWarpsPerCta);
+  k_pack<<<blocks, kWarpsPerCta * 32, 0, stream>>>(w, k, R, C, bases, units, esc_off);
+  k_scan<<<1, 1024, 0, stream>>>(esc_off, NU);
+  return cudaGetLastError() == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+}

@@ -15,6 +15,7 @@ STATUS_NAMES = {
     -1: "bad argument", -2: "bad shape", -3: "impossible geometry", -4: "pointer not 16-byte aligned",
     -5: "token count out of range", -6: "shared memory above device limit", -8: "kernel launch failed",
     -9: "cluster shape not schedulable", -10: "device is not sm_100", -11: "buffer too small",
+    -12: "matrix too tall for the allocation-free packer's fixed scratch (n > 16384)",
     -100: "tensor-map encode failed",
 }
 
@@ -53,6 +54,7 @@ SIGNATURES = [
     ("mbp_status", _I, [ctypes.POINTER(ctypes.c_int), _I]),
     ("mbp_pack_c12_workspace", _SZ, [_I, _I]),
     ("mbp_pack_c12", _I, [_P, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
+    ("mbp_pack_c12_noalloc", _I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     ("mbp_pack_c12_escapes", _I, [_P, _I, _I, _P, _P, _P, _P]),
     ("mbp_unpack_c12", _I, [ctypes.POINTER(C12), _P, _P]),
     ("mbp_pack_hilo", _I, [_P, _I, _I, _P, _P]),
