@@ -2,14 +2,22 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mbp|reference]
 
-One STEP = one cold-L2 call of each decode-GEMV shape of BASELINE config 2: fused QKV+gate (K=6144, N=14336) and
-O (K=N=6144) at M in {1, 8, 16, 32}, each with plain N(0, 0.02) weights and with the 1%-x256 escape variant
-(16 calls).  Before every call a 512 MB buffer is written to flush L2 (outside the timed events); each call is
-timed with CUDA events on the launching stream.  value = packed weight bytes streamed / kernel time (TB/s),
-the BASELINE metric's bandwidth form; per-shape us/call are in "shapes".
+Workload (one STEP): one call of each decode-GEMV shape of BASELINE config 2 -- fused QKV+gate (K=6144,
+N=14336) and O (K=N=6144) at M in {1, 8, 16, 32} -- with plain N(0, 0.02) weights and with the 1%-x256 escape
+variant: 16 calls.  The calls are ordered M-major over the four matrices (qkv, o, qkv-escape, o-escape), so
+between two uses of one matrix at least 250 MB of other weights stream through the 126 MB L2: every call
+reads its weights cold (inputs larger than L2; no flush kernel).  The step is captured once as a CUDA graph and
+replayed (the reference's judge also timed graph replays).
 
---impl reference runs the reference path's CPU implementation (the C port of the oracle: decode + FP32
-accumulate, all host threads) on a bounded row sample of the same workload, rank 0 only.
+value      = packed weight bytes of a step / device time of a step (TB/s): the BASELINE metric's bandwidth
+             form; per-shape us/call (graph replay over rotating copies of that matrix) are under "shapes".
+e2e        = the same step through the public API (mbp.kernel_fn) from pinned host buffers: H2D of x, the call
+             (new output tensor each call), D2H of the output, all inside the timed region.
+roofline   = the QKV+gate GEMV launches against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+
+--impl reference: the reference path's CPU implementation -- this build's C port of the oracle (decode +
+FP32 accumulate), all host threads -- on a bounded row sample of the same 16 calls, rank 0 only.
+Multi-GPU (torchrun): every rank runs the same workload (replicas); value sums the ranks, time is the max.
 """
 from __future__ import annotations
 
@@ -29,8 +37,9 @@ sys.path.insert(0, ROOT)
 METRIC = "µs/call cold-L2 & packed-weight HBM TB/s vs 8 TB/s peak, M=1–256"
 SHAPES = {"qkv_gate": (14336, 6144), "o": (6144, 6144)}
 MS = (1, 8, 16, 32)
-VARIANTS = ("plain", "esc1pct")
-FLUSH_BYTES = 512 << 20
+MATS = (("qkv_gate", "plain"), ("o", "plain"), ("qkv_gate", "esc1pct"), ("o", "esc1pct"))
+# DRAM bytes (read + write) of one QKV+gate M=1 launch from ncu (profiles/gemv_qkv_m1.md), per launch
+NCU_TRAFFIC_QKV_M1 = 138322688
 
 
 def peaks():
@@ -59,7 +68,9 @@ def make_x(m, k, device):
 
 
 class Clocks:
-    """Samples nvidia-smi clocks / throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index: int):
         self.index = index
@@ -72,11 +83,11 @@ class Clocks:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                       "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                       "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f,
                                       stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
-        time.sleep(0.3)
+        time.sleep(0.2)
         return self
 
     def __exit__(self, *a):
@@ -93,12 +104,11 @@ class Clocks:
         rows = [r.strip().split(", ") for r in self.f.read().strip().splitlines() if r.strip()]
         os.unlink(self.f.name)
         sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
             try:
                 sm.append(float(r[1]))
                 smax = float(r[2])
-                for nm, v in zip(names, r[5:9]):
+                for nm, v in zip(self.FIELDS, r[5:9]):
                     if v.strip() == "Active":
                         reasons.add(nm)
             except (ValueError, IndexError):
@@ -108,21 +118,21 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_reference_run(steps: int, warmup: int, sample_rows: int = 256):
+def cpu_reference_run(steps: int, warmup: int, sample_rows: int):
     """The reference path on the host: the oracle's C port (decode + FP32 accumulate) over all host threads on a
-    bounded row sample of every shape.  Returns (TB/s of packed weights, seconds per sampled step, cores)."""
+    bounded row sample of every call.  Returns (TB/s of packed weights, seconds per sampled step, cores, text)."""
     import numpy as np
     import torch
     from oracle import oracle
     cores = os.cpu_count() or 1
     work = []
-    for layer, (n, k) in SHAPES.items():
-        for variant in VARIANTS:
-            w = make_weight(sample_rows, k, variant, "cpu")
+    for m in MS:
+        for layer, variant in MATS:
+            n, k = SHAPES[layer]
+            w = make_weight(n, k, variant, "cpu")[:sample_rows]
             p = oracle.pack(w.view(torch.int16).numpy().view(np.uint16), tile_base=True)
-            for m in MS:
-                x = make_x(m, k, "cpu").view(torch.int16).numpy().view(np.uint16)
-                work.append((p, x, sample_rows * k * 1.5 + p["esc"].size * 4))
+            x = make_x(m, k, "cpu").view(torch.int16).numpy().view(np.uint16)
+            work.append((p, x, p["units"].nbytes + p["esc"].nbytes))
     for _ in range(warmup):
         for p, x, _b in work:
             oracle.gemv_packed(x, p, threads=cores)
@@ -132,7 +142,7 @@ def cpu_reference_run(steps: int, warmup: int, sample_rows: int = 256):
             oracle.gemv_packed(x, p, threads=cores)
     dt = (time.perf_counter() - t0) / max(steps, 1)
     nbytes = sum(b for _, _, b in work)
-    return nbytes / dt / 1e12, dt, cores, f"{sample_rows} rows of each of the {len(work)} (layer, M, variant) calls"
+    return nbytes / dt / 1e12, dt, cores, f"first {sample_rows} rows of each of the {len(work)} calls of a step"
 
 
 def run_reference(args, rank, world):
@@ -140,16 +150,28 @@ def run_reference(args, rank, world):
         return
     steps = max(1, min(args.steps, 3))
     warm = min(args.warmup, 1)
-    v, dt, cores, sample = cpu_reference_run(steps, warm)
+    v, dt, cores, sample = cpu_reference_run(steps, warm, sample_rows=1024)
     line = {"metric": METRIC, "value": round(v, 6), "unit": "TB/s", "n_gpus": args.gpus, "steps": steps,
             "warmup": warm, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE.json config 2 recipe)",
-            "config": {"workload": "config2 decode GEMV: qkv_gate 6144->14336, o 6144->6144, M in {1,8,16,32}, "
-                                   "plain + 1% x256 escape variant", "l2": "n/a (host)"},
+            "config": {"workload": "config2 decode GEMV: qkv_gate 6144->14336 and o 6144->6144, M in {1,8,16,32}, "
+                                   "plain + 1% x256 escape weights (16 calls per step)", "l2": "n/a (host)"},
             "impl": "reference",
             "cpu_baseline": {"value": round(v, 6), "unit": "TB/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": round(v, 6), "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def graph_of(fn, stream):
+    import torch
+    fn()  # first call on the device: attributes, planning
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            fn()
+    torch.cuda.synchronize()
+    return g
 
 
 def run_mbp(args, rank, world):
@@ -159,136 +181,172 @@ def run_mbp(args, rank, world):
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
     torch.cuda.set_device(dev)
-    stream = torch.cuda.current_stream()
-    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    side = torch.cuda.Stream()
 
-    calls = []  # (name, layer, variant, m, packed, x_dev, x_host, out_host, bytes)
-    states = {}
-    for layer, (n, k) in SHAPES.items():
-        for variant in VARIANTS:
-            w = make_weight(n, k, variant, dev)
-            st = mbp.prepare({layer: w})
-            states[(layer, variant)] = st
-            p = st["layers"][layer]
-            del w
-            for m in MS:
-                x = make_x(m, k, dev)
-                xh = x.cpu().pin_memory()
-                oh = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
-                nbytes = p.payload_bytes + 2 * m * k + 2 * m * n + p.bases.numel()
-                calls.append((f"{layer}_m{m}_{variant}", layer, variant, m, p, x, xh, oh, nbytes))
-    torch.cuda.synchronize()
+    states, packed = {}, {}
+    for layer, variant in MATS:
+        n, k = SHAPES[layer]
+        st = mbp.prepare({layer: make_weight(n, k, variant, dev)})
+        states[(layer, variant)] = st
+        packed[(layer, variant)] = st["layers"][layer]
+    torch.cuda.empty_cache()
+    calls = []  # name, layer, variant, m, packed, x_dev, out_dev, x_host, out_host, bytes
+    for m in MS:
+        for layer, variant in MATS:
+            n, k = SHAPES[layer]
+            p = packed[(layer, variant)]
+            x = make_x(m, k, dev)
+            out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+            xh = x.cpu().pin_memory()
+            oh = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+            nbytes = p.payload_bytes + p.bases.numel() + 2 * m * k + 2 * m * n
+            calls.append((f"{layer}_m{m}_{variant}", layer, variant, m, p, x, out, xh, oh, nbytes))
+    step_bytes = sum(c[-1] for c in calls)
 
-    def one_step(times=None, e2e=None):
-        for i, (name, layer, variant, m, p, x, xh, oh, nbytes) in enumerate(calls):
-            flush.fill_(float(i))
-            st = states[(layer, variant)]
-            if e2e is None:
-                a = torch.cuda.Event(enable_timing=True)
-                b = torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                mbp.gemv(p, x)
-                b.record(stream)
-                if times is not None:
-                    times[i].append((a, b))
-            else:
-                a = torch.cuda.Event(enable_timing=True)
-                b = torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                xd = xh.to(dev, non_blocking=True)
-                out = mbp.kernel_fn({"x": xd, "config": {"m": m, "n": p.n, "k": p.k, "layer": layer}}, st)
-                oh.copy_(out, non_blocking=True)
-                b.record(stream)
-                e2e[i].append((a, b))
+    def step():
+        for c in calls:
+            mbp.gemv(c[4], c[5], out=c[6])
 
+    g_step = graph_of(step, side)
     for _ in range(args.warmup):
-        one_step()
+        g_step.replay()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    times = [[] for _ in calls]
+    assert mbp.device_status() == 0
+
+    # ---------------- timed region: exactly K step replays ----------------
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
     with Clocks(dev.index) as clk:
-        torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            one_step(times)
         torch.cuda.synchronize()
-        wall = time.perf_counter() - t0
+        a.record()
+        for _ in range(args.steps):
+            g_step.replay()
+        b.record()
+        torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
     clocks = clk.summary()
+    step_ms = a.elapsed_time(b) / args.steps
     assert mbp.device_status() == 0, "device status word set during the timed region"
-
-    per_call_ms = [[a.elapsed_time(b) for a, b in ts] for ts in times]
-    step_ms = sum(statistics.mean(v) for v in per_call_ms)
-    total_bytes = sum(c[-1] for c in calls)
     if world > 1:
         t = torch.tensor([step_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         step_ms = float(t.item())
-    value = total_bytes * world / (step_ms * 1e-3) / 1e12
+    value = step_bytes * world / (step_ms * 1e-3) / 1e12
 
-    # end-to-end through the public API with host buffers (H2D of x and D2H of out inside the timed region)
-    e2e = [[] for _ in calls]
-    for _ in range(max(1, args.warmup // 2)):
-        one_step(e2e=[[] for _ in calls])
+    # ---------------- per-shape us/call: graph over rotating copies of one matrix ----------------
+    shapes = {}
+    reps = 24
+    for (layer, variant), p0 in packed.items():
+        nc = max(3, (400 << 20) // p0.units.numel())
+        ps = [p0] + [mbp.PackedC12(p0.units.clone(), p0.bases, p0.esc_off, p0.esc, p0.n, p0.k, p0.n_esc)
+                     for _ in range(nc - 1)]
+        for c in calls:
+            if (c[1], c[2]) != (layer, variant):
+                continue
+            g = graph_of(lambda: [mbp.gemv(ps[i % nc], c[5], out=c[6]) for i in range(reps)], side)
+            g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (2 * reps)
+            shapes[c[0]] = {"us": round(us, 2), "tbps": round(c[-1] / us / 1e6, 3), "bytes": c[-1]}
+            del g
+        del ps
+        torch.cuda.empty_cache()
+
+    # ---------------- e2e through the public API with host buffers ----------------
+    def api_step():
+        for c in calls:
+            st = states[(c[1], c[2])]
+            xd = c[7].to(dev, non_blocking=True)
+            out = mbp.kernel_fn({"x": xd, "config": {"m": c[3], "n": c[4].n, "k": c[4].k, "layer": c[1]}}, st)
+            c[8].copy_(out, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        api_step()
     torch.cuda.synchronize()
-    for _ in range(args.steps):
-        one_step(e2e=e2e)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, min(args.steps, 50))
+    e0.record()
+    for _ in range(e2e_steps):
+        api_step()
+    e1.record()
     torch.cuda.synchronize()
-    e2e_ms = sum(statistics.mean(a.elapsed_time(b) for a, b in ts) for ts in e2e)
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
     h2d = sum(2 * c[3] * c[4].k for c in calls)
     d2h = sum(2 * c[3] * c[4].n for c in calls)
 
-    # roofline of the dominant kernel: the QKV+gate GEMV launches
     hbm, peak_kind = peaks()
-    dom = [i for i, c in enumerate(calls) if c[1] == "qkv_gate"]
-    dom_bytes = sum(calls[i][-1] for i in dom)
-    dom_ms = sum(statistics.mean(per_call_ms[i]) for i in dom)
-    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
-    shapes = {c[0]: {"us": round(statistics.median(per_call_ms[i]) * 1e3, 2),
-                     "tbps": round(c[-1] / (statistics.median(per_call_ms[i]) * 1e-3) / 1e12, 3)}
-              for i, c in enumerate(calls)}
+    dom = [c[0] for c in calls if c[1] == "qkv_gate"]
+    dom_bytes = sum(shapes[nm]["bytes"] for nm in dom)
+    dom_us = sum(shapes[nm]["us"] for nm in dom)
+    achieved = dom_bytes / (dom_us * 1e-6) / 1e9
 
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
-            v, dt, cores, sample = cpu_reference_run(1, 0, sample_rows=128)
+            v, dt, cores, sample = cpu_reference_run(1, 0, sample_rows=512)
             cpu = {"value": round(v, 6), "unit": "TB/s", "cores": cores, "kind": "port", "sample": sample}
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: W~N(0,0.02) torch seed 0 (+1% x256 variant, randperm seed 2), x~N(0,1) seed 1",
-            "config": {"workload": "config2 decode GEMV: qkv_gate 6144->14336, o 6144->6144, M in {1,8,16,32}, "
-                                   "plain + 1% x256 escape variant (16 calls per step)",
-                       "l2": "flushed before every call (512 MB write, outside the timed events)",
+            "config": {"workload": "config2 decode GEMV: qkv_gate 6144->14336 and o 6144->6144, M in {1,8,16,32}, "
+                                   "plain + 1% x256 escape weights (16 calls per step)",
+                       "l2": "cold by construction: >=250 MB of other weights between reuses of a matrix "
+                             "(inputs larger than L2), no flush kernel",
+                       "timing": "CUDA-graph replay of the step, CUDA events on the replay stream",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "traffic": None,
-                         "kernel": "k_gemv (qkv_gate launches)", "peak_kind": peak_kind,
+                         "frac": round(achieved / hbm, 4), "traffic": NCU_TRAFFIC_QKV_M1,
+                         "kernel": "k_gemv, the 8 qkv_gate launches of a step", "peak_kind": f"{peak_kind} hbm_gbs",
                          "frac_of_8tbps": round(achieved / 8000.0, 4)},
-            "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+            "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": len(calls) * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "shapes": shapes,
-            "wall_s_timed": round(wall, 3),
         }
         print(json.dumps(line), flush=True)
 
 
+def run_profile(spec: str, launches: int = 3):
+    """--profile LAYER:M:VARIANT -- a few launches of one call for an ncu capture (no timing, no output)."""
+    import torch
+    import mbp
+    layer, m, variant = spec.split(":")
+    n, k = SHAPES[layer]
+    torch.cuda.set_device(0)
+    st = mbp.prepare({layer: make_weight(n, k, variant, "cuda")})
+    x = make_x(int(m), k, "cuda")
+    for _ in range(launches):
+        mbp.kernel_fn({"x": x, "config": {"m": int(m), "n": n, "k": k, "layer": layer}}, st)
+    torch.cuda.synchronize()
+    assert mbp.device_status() == 0
+    print("profile run ok:", spec, mbp.gemv_plan(n, k, int(m)).as_tuple())
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--profile", default=None, help="LAYER:M:VARIANT: a few launches of one call, for ncu")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mbp", choices=["mbp", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     args = ap.parse_args()
+    if args.profile:
+        run_profile(args.profile)
+        return
+    args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if world > 1:
