@@ -129,6 +129,15 @@ int mbp_gemv_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t
 int mbp_gemv_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
                      const mbp_gemv_geom* geom, cudaStream_t stream);
 
+/* ---- verify-path GEMM on the tcgen05 tensor cores, weights unpacked in shared memory (replaces the dense
+ * BF16 verify GEMMs ss_gemm S:783, q_kernel S:979 / qb_kernel S:4576, ol_projection S:1547, projection
+ * S:2985, and the out-of-scope cuBLASLt routes S:2309-2376): out[m, n_out] = x . W[0:n_out]^T, FP32
+ * accumulation in TMEM, any m >= 1 (tiles of up to 256 tokens; intended for m > 32). ---- */
+int mbp_gemm_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo,
+                 cudaStream_t stream);
+int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
+                     cudaStream_t stream);
+
 /* ---- FP32 router through the hi/lo pair (replaces rr_launch / rr_scalar / rr_small S:856-861, routertail
  * S:5424, rwdl S:5377): out_f32[m, n] = x . hi^T + x . lo^T, FP32 accumulation. ---- */
 int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,

@@ -3,6 +3,7 @@
 
 int mbp_status_pack(int* v, int clear);
 int mbp_status_gemv(int* v, int clear);
+int mbp_status_gemm(int* v, int clear);
 
 extern "C" {
 
@@ -22,6 +23,7 @@ int mbp_status(int* status, int clear) {
   *status = 0;
   int rc = mbp_status_pack(status, clear);
   if (rc == MBP_OK) rc = mbp_status_gemv(status, clear);
+  if (rc == MBP_OK) rc = mbp_status_gemm(status, clear);
   return rc;
 }
 

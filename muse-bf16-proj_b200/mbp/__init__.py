@@ -5,9 +5,10 @@ Reference (NathenFernandes/muse-bf16-proj, submission.py): types ``Weights`` / `
 
 * ``prepare`` packs every BF16 layer into the lossless 12-bit format on the GPU and the FP32 router into a BF16
   hi/lo pair, checks the packing round trip bit for bit on the device, and returns the state.
-* ``kernel_fn`` routes one call to one kernel launch: the weight-streaming GEMV (any M, 32-token blocks) for BF16
-  layers and the hi/lo GEMV for the router, writing a NEW output tensor ``[m, n]`` (BF16, FP32 for the
-  router) like the reference (README.md:36; S:404, S:889).
+* ``kernel_fn`` routes one call to one kernel launch: the weight-streaming GEMV for BF16 layers at m <= 32
+  (the reference's decode routes), the tcgen05 verify GEMM at m > 32 (its verify routes), and the hi/lo GEMV
+  for the router, writing a NEW output tensor ``[m, n]`` (BF16, FP32 for the router) like the reference
+  (README.md:36; S:404, S:889).
 
 Unlike the reference there is no fallback: an unsupported call raises instead of dropping to SGLang.
 """
@@ -18,13 +19,14 @@ from typing import TypedDict
 import torch
 
 from ._lib import MbpError, device_status, lib
-from .ops import (BASE_MATRIX, BASE_TILE, PackedC12, PackedHiLo, gemv, gemv_plan, pack_c12, pack_hilo, router,
-                  unpack_c12)
+from .ops import (BASE_MATRIX, BASE_TILE, PackedC12, PackedHiLo, gemm, gemv, gemv_plan, pack_c12, pack_hilo,
+                  router, unpack_c12)
 
 __all__ = ["Weights", "Config", "Inputs", "prepare", "kernel_fn", "MbpError", "PackedC12", "PackedHiLo", "pack_c12",
-           "unpack_c12", "pack_hilo", "gemv", "gemv_plan", "router", "device_status", "BASE_MATRIX", "BASE_TILE"]
+           "unpack_c12", "pack_hilo", "gemv", "gemm", "gemv_plan", "router", "device_status", "BASE_MATRIX", "BASE_TILE"]
 
 LAYERS = ("qkv_gate", "o", "pooler", "unpooler", "router")
+GEMV_MAX_M = 32  # the reference's decode/verify boundary: small-M GEMVs up to 32 tokens (SM_MAX_M, S:252)
 
 
 class Weights(TypedDict):
@@ -90,4 +92,4 @@ def kernel_fn(data: Inputs, state: dict) -> torch.Tensor:
         raise KeyError(f"layer {layer!r} was not prepared")
     if not 0 < n <= p.n or n % 16:
         raise ValueError(f"n={n} must be a multiple of 16 in (0, {p.n}]")
-    return gemv(p, x, n_out=n)
+    return gemv(p, x, n_out=n) if x.shape[0] <= GEMV_MAX_M else gemm(p, x, n_out=n)

@@ -145,6 +145,23 @@ def gemv(p: PackedC12, x: torch.Tensor, n_out: int | None = None, out: torch.Ten
     return out
 
 
+def gemm(p: PackedC12, x: torch.Tensor, n_out: int | None = None, out: torch.Tensor | None = None,
+         out_dtype=torch.bfloat16) -> torch.Tensor:
+    """out[m, n_out] = x . W[:n_out]^T through the tcgen05 verify GEMM (replaces S:783/979/1547/2985)."""
+    n_out = p.n if n_out is None else n_out
+    _check_x(x, p.k, p.units.device)
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty((m, n_out), dtype=out_dtype, device=x.device)
+    if out.dim() != 2 or out.shape[0] != m or out.shape[1] < n_out or out.stride(1) != 1:
+        raise ValueError("bad out tensor")
+    if out.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"unsupported output dtype {out.dtype}")
+    fn = lib().mbp_gemm_c12_f32 if out.dtype == torch.float32 else lib().mbp_gemm_c12
+    check(fn(ctypes.byref(p.desc), _ptr(x), m, n_out, _ptr(out), out.stride(0), _stream()), "mbp_gemm_c12")
+    return out
+
+
 def router(p: PackedHiLo, x: torch.Tensor, out: torch.Tensor | None = None, geom: Geom | None = None):
     """out_f32[m, n] = x . (hi + lo)^T (replaces rr_launch / rr_scalar / rr_small, S:856-861)."""
     _check_x(x, p.k, p.units.device)

@@ -1,0 +1,83 @@
+"""tcgen05 verify GEMM parity on the GPU through the C ABI.
+
+* one-hot exactness (the reference's sm_verify_onehot idea, S:281-294): rows of x = e_k reproduce W[:, k] bit
+  for bit, which pins the decode into shared memory, the swizzled operand layout, the UMMA descriptors and the
+  TMEM epilogue mapping;
+* BASELINE config 3 shapes (M in {128, 256}; QKV+gate, O, pooler 6144->1536, unpooler 1536->6144) against the
+  FP32 reference at rtol 1e-2 / atol 1e-2 plus the reference's norm rule (S:297-317);
+* ragged token counts (tiles of up to 256 tokens, token tails), n_out < n, escape-heavy weights, FP32 output.
+"""
+import pytest
+import torch
+
+from helpers import assert_close_bf16, assert_reference_norms, tokens, weight
+
+pytestmark = pytest.mark.gpu
+
+CONFIG3 = {"qkv_gate": (14336, 6144), "o": (6144, 6144), "pooler": (1536, 6144), "unpooler": (6144, 1536)}
+
+
+def ref_f32(x, w, n_out=None):
+    n_out = w.shape[0] if n_out is None else n_out
+    return x.float() @ w[:n_out].float().T
+
+
+def test_gemm_onehot_exact():
+    import mbp
+    w = weight(384, 1024, seed=21, escape_frac=0.01)
+    p = mbp.pack_c12(w)
+    for start in range(0, 1024, 256):
+        x = torch.zeros(256, 1024, dtype=torch.bfloat16, device="cuda")
+        x[torch.arange(256), torch.arange(start, start + 256)] = 1.0
+        out = mbp.gemm(p, x)
+        assert torch.equal(out.view(torch.int16), w[:, start:start + 256].T.contiguous().view(torch.int16)), start
+    assert mbp.device_status() == 0
+
+
+@pytest.mark.parametrize("layer", list(CONFIG3))
+@pytest.mark.parametrize("m", [128, 256])
+def test_gemm_baseline_config3(layer, m):
+    import mbp
+    n, k = CONFIG3[layer]
+    w = weight(n, k, seed=0)
+    p = mbp.pack_c12(w)
+    x = tokens(m, k, seed=m)
+    out = mbp.gemm(p, x)
+    torch.cuda.synchronize()
+    assert mbp.device_status() == 0
+    ref = ref_f32(x, w)
+    assert_close_bf16(out, ref)
+    assert_reference_norms(out, ref)
+
+
+@pytest.mark.parametrize("m", [1, 17, 33, 48, 100, 200, 255, 257, 300, 512])
+def test_gemm_token_counts(m):
+    import mbp
+    w = weight(1024, 2048, seed=m, escape_frac=0.005)
+    p = mbp.pack_c12(w)
+    x = tokens(m, 2048, seed=m + 1)
+    out = mbp.gemm(p, x)
+    assert_close_bf16(out, ref_f32(x, w))
+
+
+def test_gemm_partial_rows_and_f32():
+    import mbp
+    w = weight(8192, 1024, seed=5, escape_frac=0.01)
+    p = mbp.pack_c12(w)
+    x = tokens(160, 1024, seed=6)
+    out = mbp.gemm(p, x, n_out=1040)  # not a multiple of the 128-row CTA tile
+    assert out.shape == (160, 1040)
+    assert_close_bf16(out, ref_f32(x, w, 1040))
+    o32 = mbp.gemm(p, x, out_dtype=torch.float32)
+    assert torch.allclose(o32, ref_f32(x, w), rtol=1e-4, atol=1e-3)
+
+
+def test_gemm_matches_gemv():
+    """Both kernels compute the same FP32-accumulated products (different summation order)."""
+    import mbp
+    w = weight(2048, 3072, seed=8, escape_frac=0.01)
+    p = mbp.pack_c12(w)
+    x = tokens(32, 3072, seed=9)
+    a = mbp.gemm(p, x, out_dtype=torch.float32)
+    b = mbp.gemv(p, x, out_dtype=torch.float32)
+    assert torch.allclose(a, b, rtol=1e-4, atol=1e-3)
