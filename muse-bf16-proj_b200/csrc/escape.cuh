@@ -34,6 +34,21 @@ struct EscCursor {
     next_chunk = esc_chunk(__shfl_sync(0xffffffffu, win0, 0));
   }
 
+  // Skips the entries of chunks below c (chunks this warp does not process).  Warp-uniform.
+  MBP_DEV void seek(uint32_t c, int lane) {
+    while (next_chunk < c) {
+      const int i = ep - wbase;
+      const bool below = lane >= i && esc_chunk(win0) < c;
+      ep += __popc(__ballot_sync(0xffffffffu, below));
+      if (ep - wbase >= 32) {
+        wbase += 32;
+        win0 = win1;
+        win1 = (wbase + 32 + lane < eend) ? __ldg(esc + wbase + 32 + lane) : kEscSentinel;
+      }
+      next_chunk = esc_chunk(__shfl_sync(0xffffffffu, win0, (ep - wbase) & 31));
+    }
+  }
+
   // Applies the escapes of chunk c to the decoded registers A. Warp-uniform; `xr` = this warp's mask region.
   MBP_DEV void apply(uint32_t c, uint32_t (&A)[16], uint32_t xr, int lane) {
     if (next_chunk != c) return;

@@ -5,15 +5,17 @@
 // S:979<25-170>, qb_kernel S:4576, ol_projection S:1547<18-106>, projection S:2985) and its cuBLASLt routes
 // (S:2309-2376, out of scope), which read unpacked BF16 weights; here the weights stay packed in HBM.
 //
-// CTA tile: 128 weight rows (8 row tiles) x BN tokens (<= 256), full K.  Warp roles:
-//   warp 0      TMA producer: per 64-column chunk, one 3-D box of 8 packed units (12 KB) and one 2-D box of
-//               the x tile (BN rows x 128 bytes, 128-byte swizzle), each completing on its ring's mbarrier;
-//   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN, K=16, BF16 -> FP32) x4 per chunk,
-//               A = decoded weights and B = x, both K-major SW128 shared-memory descriptors; tcgen05.commit
-//               frees the A and x stages and finally signals the accumulator;
-//   warps 2-9   decoders: warp d decodes row tile d of each chunk in registers (same decode and escape cursor
-//               as the GEMV), stores it into the A stage in the canonical SW128 K-major layout and fences it
-//               to the async proxy; afterwards they read the accumulator (tcgen05.ld 32x32b) and store BF16.
+// CTA tile: 128 weight rows (8 row tiles) x BN tokens (<= 256) x a K range; `split` CTAs of a cluster share
+// one tile's K range and reduce through distributed shared memory.  Warp roles:
+//   warp 0       TMA producer: per 64-column chunk, one 3-D box of 8 packed units (12 KB) and one 2-D box of
+//                the x tile (BN rows x 128 bytes, 128-byte swizzle), each completing on its ring's mbarrier;
+//   warp 1       allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN, K=16, BF16 -> FP32) x4 per chunk,
+//                A = decoded weights and B = x, both K-major SW128 shared-memory descriptors; tcgen05.commit
+//                frees the A and x stages and finally signals the accumulator;
+//   warps 2-17   decoders in kGroups groups of 8 warps; group g handles every kGroups-th chunk, warp d of a
+//                group decodes row tile d in registers (same decode and escape cursor as the GEMV), stores it
+//                into the A stage in the canonical SW128 K-major layout and fences it to the async proxy.
+//                Afterwards they read the accumulator (tcgen05.ld 32x32b) and store (or cluster-reduce) it.
 // All waits are bounded; TMEM is always released.
 #include "common.cuh"
 #include "escape.cuh"
@@ -21,18 +23,21 @@
 
 #include <map>
 #include <mutex>
+#include <tuple>
 
 using namespace mbp;
 
 namespace {
 
-constexpr int kThreads = 320;  // 10 warps
-constexpr int kDecWarps = 8;
-constexpr int kPS = 4;         // packed ring depth
-constexpr int kAS = 3;         // decoded-A ring depth
-constexpr int kXS = 3;         // x ring depth
+constexpr int kGroups = 2;                 // decoder groups working on alternate chunks
+constexpr int kDecWarps = 8 * kGroups;
+constexpr int kThreads = 32 * (2 + kDecWarps);
+constexpr int kPS = 4;                     // packed ring depth
+constexpr int kAS = 3;                     // decoded-A ring depth
+constexpr int kXS = 2;                     // x ring depth (x tiles come from L2)
 constexpr int kPackedStage = 8 * MBP_C12_UNIT_BYTES;  // 12 KB
 constexpr int kAStage = 128 * 128;                    // 128 rows x 64 bf16
+constexpr int kMaxSmem = 227 * 1024;
 
 struct __align__(64) GemmParams {
   CUtensorMap wmap;  // units as [R][C][192 x u64], box {192, 1, 8}
@@ -41,7 +46,7 @@ struct __align__(64) GemmParams {
   const int32_t* esc_off;
   const uint32_t* esc;
   void* out;
-  int C, Rout, m, ldo, bn;
+  int C, Rout, m, ldo, bn, split;
   int f32out;
 };
 
@@ -52,9 +57,9 @@ struct GLayout {
 __host__ __device__ inline GLayout gemm_layout(int bn) {
   GLayout L;
   L.packed = 0;
-  L.a = L.packed + kPS * kPackedStage;              // multiple of 1024
-  L.x = L.a + kAS * kAStage;                        // multiple of 1024
-  L.xr = L.x + kXS * bn * 128;                      // bn multiple of 16 -> multiple of 2048
+  L.a = L.packed + kPS * kPackedStage;  // multiple of 1024
+  L.x = L.a + kAS * kAStage;            // multiple of 1024
+  L.xr = L.x + kXS * bn * 128;          // bn multiple of 16 -> multiple of 2048
   L.bars = L.xr + kDecWarps * kXorWarpBytes;
   L.tmem_slot = L.bars + 8 * (2 * kPS + 2 * kAS + 2 * kXS + 1);
   L.total = L.tmem_slot + 16;
@@ -108,6 +113,13 @@ MBP_DEV void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+MBP_DEV void store_elem(const GemmParams& p, int tok, int row, float f) {
+  if (p.f32out)
+    reinterpret_cast<float*>(p.out)[(size_t)tok * p.ldo + row] = f;
+  else
+    reinterpret_cast<uint16_t*>(p.out)[(size_t)tok * p.ldo + row] = __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
 __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ GemmParams p) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -124,15 +136,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   const int C = p.C;
   const int rb0 = blockIdx.x * 8;  // first row tile
   const int tok0 = blockIdx.y * p.bn;
+  const int ks = blockIdx.z;       // K split index == cluster rank (cluster dims 1 x 1 x split)
+  const int cs = (int)((long long)ks * C / p.split), ce = (int)((long long)(ks + 1) * C / p.split);
+  const int nc = ce - cs;
   const uint32_t tmem_cols = p.bn <= 32 ? 32 : p.bn <= 64 ? 64 : p.bn <= 128 ? 128 : 256;
 
   if (tid == 0) {
     for (int i = 0; i < kPS; ++i) {
       mbar_init(pfull + 8 * i, 1);
-      mbar_init(pempty + 8 * i, kDecWarps * 32);
+      mbar_init(pempty + 8 * i, 8 * 32);
     }
     for (int i = 0; i < kAS; ++i) {
-      mbar_init(afull + 8 * i, kDecWarps * 32);
+      mbar_init(afull + 8 * i, 8 * 32);
       mbar_init(aempty + 8 * i, 1);
     }
     for (int i = 0; i < kXS; ++i) {
@@ -158,29 +173,29 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      for (int c = 0; c < C; ++c) {
-        const int ps = c % kPS, xs = c % kXS;
-        if (c >= kPS && !mbar_wait(pempty + 8 * ps, ((c / kPS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
+      for (int i = 0; i < nc; ++i) {
+        const int ps = i % kPS, xs = i % kXS;
+        if (i >= kPS && !mbar_wait(pempty + 8 * ps, ((i / kPS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
         mbar_arrive_expect_tx(pfull + 8 * ps, kPackedStage);
-        tma_load_3d(base + L.packed + ps * kPackedStage, &p.wmap, 0, c, rb0, pfull + 8 * ps);
-        if (c >= kXS && !mbar_wait(xempty + 8 * xs, ((c / kXS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
+        tma_load_3d(base + L.packed + ps * kPackedStage, &p.wmap, 0, cs + i, rb0, pfull + 8 * ps);
+        if (i >= kXS && !mbar_wait(xempty + 8 * xs, ((i / kXS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
         mbar_arrive_expect_tx(xfull + 8 * xs, (uint32_t)p.bn * 128);
-        tma_load_2d(base + L.x + xs * p.bn * 128, &p.xmap, c * 64, tok0, xfull + 8 * xs);
+        tma_load_2d(base + L.x + xs * p.bn * 128, &p.xmap, (cs + i) * 64, tok0, xfull + 8 * xs);
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16(p.bn);
-      for (int c = 0; c < C; ++c) {
-        const int as = c % kAS, xs = c % kXS;
-        if (!mbar_wait(afull + 8 * as, (c / kAS) & 1, MBP_DEV_TIMEOUT_FULL)) break;
-        if (!mbar_wait(xfull + 8 * xs, (c / kXS) & 1, MBP_DEV_TIMEOUT_FULL)) break;
+      for (int i = 0; i < nc; ++i) {
+        const int as = i % kAS, xs = i % kXS;
+        if (!mbar_wait(afull + 8 * as, (i / kAS) & 1, MBP_DEV_TIMEOUT_FULL)) break;
+        if (!mbar_wait(xfull + 8 * xs, (i / kXS) & 1, MBP_DEV_TIMEOUT_FULL)) break;
         tc_fence_after();
         const uint32_t a0 = base + L.a + as * kAStage, b0 = base + L.x + xs * p.bn * 128;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc_mma(tmem, smem_desc_sw128(a0 + 32 * k), smem_desc_sw128(b0 + 32 * k), idesc, (c | k) != 0);
+          tc_mma(tmem, smem_desc_sw128(a0 + 32 * k), smem_desc_sw128(b0 + 32 * k), idesc, (i | k) != 0);
         tc_commit(aempty + 8 * as);
         tc_commit(xempty + 8 * xs);
       }
@@ -188,19 +203,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     }
     __syncwarp();
   } else {
-    // ---------------- decoders ----------------
-    const int d = warp - 2;  // row tile within the block
+    // ---------------- decoders: group gi takes local chunks gi, gi + kGroups, ... ----------------
+    const int dw = warp - 2, gi = dw >> 3, d = dw & 7;
     const int rt = rb0 + d;
     const bool valid = rt < p.Rout;
     uint32_t T0 = 0, T1 = 0;
     EscCursor cur;
-    const uint32_t xr = base + L.xr + d * kXorWarpBytes;
+    const uint32_t xr = base + L.xr + dw * kXorWarpBytes;
     xor_mask_clear(xr, lane);
     if (valid) {
       const uint32_t b = p.bases[rt];
       T0 = table_lo(b);
       T1 = table_hi(b);
-      cur.init(p.esc, p.esc_off[(size_t)rt * C], p.esc_off[(size_t)rt * C + C], lane);
+      cur.init(p.esc, p.esc_off[(size_t)rt * C + cs], p.esc_off[(size_t)rt * C + ce], lane);
     } else {
       cur.init(p.esc, 0, 0, lane);
     }
@@ -214,9 +229,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       dst[rh][0] = row + ((uint32_t)((2 * t) ^ (r & 7)) << 4);
       dst[rh][1] = row + ((uint32_t)((2 * t + 1) ^ (r & 7)) << 4);
     }
-    for (int c = 0; c < C; ++c) {
-      const int ps = c % kPS, as = c % kAS;
-      if (!mbar_wait(pfull + 8 * ps, (c / kPS) & 1, MBP_DEV_TIMEOUT_FULL)) break;
+    for (int i = gi; i < nc; i += kGroups) {
+      const int ps = i % kPS, as = i % kAS;
+      if (!mbar_wait(pfull + 8 * ps, (i / kPS) & 1, MBP_DEV_TIMEOUT_FULL)) break;
       const unsigned char* u = sm + L.packed + ps * kPackedStage + d * MBP_C12_UNIT_BYTES + lane * 16;
       const uint4 p0 = *reinterpret_cast<const uint4*>(u);
       const uint4 p1 = *reinterpret_cast<const uint4*>(u + 512);
@@ -224,8 +239,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       mbar_arrive(pempty + 8 * ps);
       uint32_t A[16];
       decode_unit(p0, p1, p2, T0, T1, A);
-      if (valid) cur.apply((uint32_t)c, A, xr, lane);
-      if (c >= kAS && !mbar_wait(aempty + 8 * as, ((c / kAS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
+      if (valid) {
+        cur.seek((uint32_t)(cs + i), lane);
+        cur.apply((uint32_t)(cs + i), A, xr, lane);
+      }
+      if (i >= kAS && !mbar_wait(aempty + 8 * as, ((i / kAS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
       unsigned char* a = sm + L.a + as * kAStage;
 #pragma unroll
       for (int rh = 0; rh < 2; ++rh) {
@@ -235,33 +253,65 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       fence_async_smem();
       mbar_arrive(afull + 8 * as);
     }
-    // ---------------- epilogue: TMEM -> registers -> global ----------------
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const int half = (warp - 2) >> 2;
-    const bool ok = mbar_wait(done, 0, MBP_DEV_TIMEOUT_MMA);
+  }
+
+  // ---------------- epilogue: TMEM -> registers -> global (or a cluster reduction) ----------------
+  // Decoder warps own TMEM lane quadrant (warp % 4); the kDecWarps/4 warps of a quadrant split the columns.
+  const bool epi = warp >= 2;
+  const int q = warp & 3, part = (warp - 2) >> 2, nparts = kDecWarps / 4;
+  const int ncol = (p.bn + 31) / 32;
+  const int row_l = q * 32 + lane;                 // row inside the 128-row tile
+  const int row = rb0 * 16 + row_l;                // global output row
+  bool ok = true;
+  if (epi) {
+    ok = mbar_wait(done, 0, MBP_DEV_TIMEOUT_MMA);
+    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
     tc_fence_after();
-    if (ok) {
-      const int row = rb0 * 16 + q * 32 + lane;
-      const int ncol = (p.bn + 31) / 32;
-      for (int cc = half; cc < ncol; cc += 2) {
+  }
+  if (p.split == 1) {
+    if (epi && ok) {
+      for (int cc = part; cc < ncol; cc += nparts) {
         uint32_t v[32];
         tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32), v);
         if (row < p.Rout * 16) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int tok = tok0 + cc * 32 + j;
-            if (tok < p.m) {
-              const float f = __uint_as_float(v[j]);
-              if (p.f32out)
-                reinterpret_cast<float*>(p.out)[(size_t)tok * p.ldo + row] = f;
-              else
-                reinterpret_cast<uint16_t*>(p.out)[(size_t)tok * p.ldo + row] =
-                    __bfloat16_as_ushort(__float2bfloat16_rn(f));
-            }
+            if (tok < p.m) store_elem(p, tok, row, __uint_as_float(v[j]));
           }
         }
       }
     }
+  } else {
+    // Partial tiles go to shared memory column-major (element (r, c) at c*128 + r, conflict-free), the ring
+    // area being free once every MMA has completed; rank ks then sums columns [c0, c1) over the cluster.
+    float* red = reinterpret_cast<float*>(sm);
+    if (epi) {
+      for (int cc = part; cc < ncol; cc += nparts) {
+        uint32_t v[32];
+        if (ok) tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32), v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) red[(cc * 32 + j) * 128 + row_l] = ok ? __uint_as_float(v[j]) : 0.f;
+      }
+    }
+    cluster_sync();
+    const int per = (ncol * 32 + p.split - 1) / p.split;
+    const int c0 = ks * per, c1 = min(ncol * 32, c0 + per);
+    const uint32_t raddr = smem_u32(red);
+    for (int idx = tid; idx < (c1 - c0) * 128; idx += kThreads) {
+      const int c = c0 + idx / 128, r = idx % 128;
+      float s = 0.f;
+      for (int rk = 0; rk < p.split; ++rk) {
+        float f;
+        asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                     : "=f"(f)
+                     : "r"(mapa(raddr + (uint32_t)(c * 128 + r) * 4, (uint32_t)rk)));
+        s += f;
+      }
+      const int tok = tok0 + c, grow = rb0 * 16 + r;
+      if (tok < p.m && grow < p.Rout * 16) store_elem(p, tok, grow, s);
+    }
+    cluster_sync();  // keep this CTA's partials alive until every rank has read them
   }
   tc_fence_before();
   __syncthreads();
@@ -284,19 +334,73 @@ bool encode_units_3d(CUtensorMap* map, const void* units, int R, int C) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-std::mutex g_attr_mu;
+std::mutex g_mu;
 std::map<int, bool> g_attr_done;
+std::map<std::tuple<int, int, int>, int> g_clusters;  // (device, split, smem) -> co-resident clusters
 
 int ensure_attr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MBP_ERR_LAUNCH;
-  std::lock_guard<std::mutex> lk(g_attr_mu);
+  std::lock_guard<std::mutex> lk(g_mu);
   if (g_attr_done.count(dev)) return MBP_OK;
   if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_gemm), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           227 * 1024) != cudaSuccess)
+                           kMaxSmem) != cudaSuccess)
     return MBP_ERR_SMEM;
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_gemm), cudaFuncAttributeNonPortableClusterSizeAllowed,
+                           1) != cudaSuccess)
+    return MBP_ERR_CLUSTER;
   g_attr_done[dev] = true;
   return MBP_OK;
+}
+
+int co_resident_ctas(int split, int smem) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const auto key = std::make_tuple(dev, split, smem);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_clusters.find(key);
+    if (it != g_clusters.end()) return it->second;
+  }
+  int ctas = sms;
+  if (split > 1) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, split);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = split;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    ctas = cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(&k_gemm), &cfg) == cudaSuccess
+               ? clusters * split
+               : 0;
+    cudaGetLastError();
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_clusters[key] = ctas;
+  return ctas;
+}
+
+// K split: the largest cluster (<= 8, >= 4 chunks per CTA) whose tiles still fit one wave of co-resident CTAs,
+// when the tile count alone leaves more than a quarter of the SMs idle.
+int choose_split(int tiles, int C, int smem) {
+  int sms = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (tiles * 4 >= sms * 3) return 1;
+  int best = 1;
+  for (int s = 2; s <= 8; ++s) {
+    if (C / s < 4) break;
+    const int cap = co_resident_ctas(s, smem);
+    if (cap >= tiles * s && tiles * s <= sms) best = s;
+  }
+  return best;
 }
 
 int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out, int ldo, bool f32,
@@ -309,7 +413,10 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u)) return MBP_ERR_ALIGN;
   const int bn = m >= 256 ? 256 : ((m + 15) / 16) * 16;
   const GLayout L = gemm_layout(bn);
-  if (L.total + 1024 > 227 * 1024) return MBP_ERR_SMEM;
+  const int smem = L.total + 1024;
+  if (smem > kMaxSmem) return MBP_ERR_SMEM;
+  // the cluster reduction reuses the ring area for a 128 x bn FP32 tile
+  if (128 * ((bn + 31) / 32) * 32 * 4 > L.xr) return MBP_ERR_SMEM;
   int rc = ensure_attr();
   if (rc) return rc;
   GemmParams p;
@@ -328,9 +435,25 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   p.ldo = ldo;
   p.bn = bn;
   p.f32out = f32 ? 1 : 0;
-  dim3 grid((p.Rout + 7) / 8, (m + bn - 1) / bn, 1);
-  k_gemm<<<grid, kThreads, L.total + 1024, stream>>>(p);
-  return cudaGetLastError() == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+  const int tiles = ((p.Rout + 7) / 8) * ((m + bn - 1) / bn);
+  p.split = choose_split(tiles, C, smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.Rout + 7) / 8, (m + bn - 1) / bn, p.split);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (p.split > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = p.split;
+    na = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, k_gemm, p) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
 }
 
 }  // namespace
