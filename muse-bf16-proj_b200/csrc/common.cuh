@@ -154,8 +154,9 @@ MBP_DEV uint32_t cluster_rank() {
   return r;
 }
 
-MBP_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
-MBP_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Non-.aligned forms: correct even if a warp reaches the barrier diverged (every thread still arrives once).
+MBP_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+MBP_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 MBP_DEV void cluster_sync() {
   cluster_arrive();
   cluster_wait();

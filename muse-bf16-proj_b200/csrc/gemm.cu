@@ -33,8 +33,14 @@ constexpr int kGroups = 2;                 // decoder groups working on alternat
 constexpr int kDecWarps = 8 * kGroups;
 constexpr int kThreads = 32 * (2 + kDecWarps);
 constexpr int kPS = 4;                     // packed ring depth
-constexpr int kAS = 3;                     // decoded-A ring depth
-constexpr int kXS = 2;                     // x ring depth (x tiles come from L2)
+constexpr int kAS = 2;                     // decoded-A ring depth
+constexpr int kXS = 3;                     // x ring depth
+// Decoder group g owns chunks i = g (mod kGroups).  A ring whose barriers the decoders wait on must give every
+// stage to a single group (depth a multiple of kGroups): otherwise a group could wait for use k+1 of a stage
+// while use k, owned by the other group and completed out of order by the TMA engine, is still pending, and
+// mbarrier parity waits, which only tell the current phase from the previous one, would return on the stale
+// phase (wrong data, and arrivals counted into the wrong phase).
+static_assert(kPS % kGroups == 0 && kAS % kGroups == 0, "ring depths must be multiples of the decoder groups");
 constexpr int kPackedStage = 8 * MBP_C12_UNIT_BYTES;  // 12 KB
 constexpr int kAStage = 128 * 128;                    // 128 rows x 64 bf16
 constexpr int kMaxSmem = 227 * 1024;
@@ -183,6 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         tma_load_2d(base + L.x + xs * p.bn * 128, &p.xmap, (cs + i) * 64, tok0, xfull + 8 * xs);
       }
     }
+    __syncwarp();  // lanes 1-31 wait here for the producing lane
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
@@ -294,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         for (int j = 0; j < 32; ++j) red[(cc * 32 + j) * 128 + row_l] = ok ? __uint_as_float(v[j]) : 0.f;
       }
     }
+    __syncthreads();  // every role of this CTA is done before the cluster barrier
     cluster_sync();
     const int per = (ncol * 32 + p.split - 1) / p.split;
     const int c0 = ks * per, c1 = min(ncol * 32, c0 + per);
@@ -316,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols) : "memory");
   }

@@ -81,3 +81,22 @@ def test_gemm_matches_gemv():
     a = mbp.gemm(p, x, out_dtype=torch.float32)
     b = mbp.gemv(p, x, out_dtype=torch.float32)
     assert torch.allclose(a, b, rtol=1e-4, atol=1e-3)
+
+
+def test_gemm_back_to_back_split_k_status():
+    """Many back-to-back launches of a cluster split-K configuration (unpooler 1536 -> 6144, K split across CTAs)
+    with no host synchronisation in between: results stay exact and no bounded wait ever gives up.  This is the
+    pattern that exposed a pipeline-phase hazard when a shared-memory ring's stages alternated between the two
+    decoder groups."""
+    import mbp
+    w = weight(6144, 1536, seed=31, escape_frac=0.01)
+    p = mbp.pack_c12(w)
+    copies = [p] + [mbp.PackedC12(p.units.clone(), p.bases, p.esc_off, p.esc, p.n, p.k, p.n_esc) for _ in range(3)]
+    x = tokens(128, 1536, seed=32)
+    ref = mbp.gemm(p, x)
+    outs = [mbp.gemm(copies[i % 4], x) for i in range(64)]
+    torch.cuda.synchronize()
+    assert mbp.device_status() == 0
+    for o in outs:
+        assert torch.equal(o, ref)
+    assert_close_bf16(ref, ref_f32(x, w))
