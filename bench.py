@@ -17,7 +17,9 @@ roofline   = the QKV+gate GEMV launches against the measured HBM copy bandwidth 
 
 --impl reference: the reference path's CPU implementation -- this build's C port of the oracle (decode +
 FP32 accumulate), all host threads -- on a bounded row sample of the same 16 calls, rank 0 only.
-Multi-GPU (torchrun): every rank runs the same workload (replicas); value sums the ranks, time is the max.
+Multi-GPU (torchrun, N > 1): the same step with every projection tensor-parallel over the N ranks (QKV+gate
+column-parallel + NCCL all-gather, O row-parallel + NCCL all-reduce): total work fixed ("strong" scaling),
+device time = max over ranks.
 """
 from __future__ import annotations
 
@@ -318,6 +320,132 @@ def run_mbp(args, rank, world):
         print(json.dumps(line), flush=True)
 
 
+def run_mbp_tp(args, rank, world):
+    """N > 1: the same 16-call step, each projection tensor-parallel over the N ranks (BASELINE config 5 layout:
+    QKV+gate column-parallel + NCCL all-gather, O row-parallel + NCCL all-reduce of FP32 partials).  Total work is
+    fixed (strong scaling); value = packed bytes of the unsharded layers per step / step time (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    import mbp
+    from mbp.tp import TPLinear
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    lins = {}
+    for layer, variant in MATS:
+        n, k = SHAPES[layer]
+        lins[(layer, variant)] = TPLinear(make_weight(n, k, variant, dev), "column" if layer == "qkv_gate" else "row")
+    torch.cuda.empty_cache()
+    shard_bytes = {key: torch.tensor([lin.payload_bytes], device=dev) for key, lin in lins.items()}
+    for t in shard_bytes.values():
+        dist.all_reduce(t)
+    calls = []
+    for m in MS:
+        for layer, variant in MATS:
+            n, k = SHAPES[layer]
+            x = make_x(m, k, dev)
+            nbytes = int(shard_bytes[(layer, variant)].item()) + 2 * m * k + 2 * m * n
+            calls.append((f"{layer}_m{m}_{variant}", lins[(layer, variant)], x, nbytes, m, n, k))
+    step_bytes = sum(c[3] for c in calls)
+
+    def step():
+        for c in calls:
+            c[1](c[2])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    g = None
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                step()
+        torch.cuda.synchronize()
+        g = graph
+    except Exception:
+        g = None
+    ok = torch.tensor([1 if g is not None else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    use_graph = int(ok.item()) == 1
+    run = (lambda: g.replay()) if use_graph else step
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index) as clk:
+        dist.barrier()
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(args.steps):
+            run()
+        b.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+    clocks = clk.summary()
+    t = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms = float(t.item())
+    assert mbp.device_status() == 0
+
+    # e2e: host x in, host output back, every call, eager
+    hx = [c[2].cpu().pin_memory() for c in calls]
+    ho = [torch.empty((c[4], c[5]), dtype=torch.bfloat16).pin_memory() for c in calls]
+
+    def api_step():
+        for c, xh, oh in zip(calls, hx, ho):
+            out = c[1](xh.to(dev, non_blocking=True))
+            oh.copy_(out, non_blocking=True)
+
+    api_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, min(args.steps, 20))
+    e0.record()
+    for _ in range(e2e_steps):
+        api_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
+    dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    hbm, peak_kind = peaks()
+    if rank == 0:
+        value = step_bytes / (step_ms * 1e-3) / 1e12
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: W~N(0,0.02) torch seed 0 (+1% x256 variant, randperm seed 2), x~N(0,1) seed 1",
+            "config": {"workload": "config2 decode GEMV step (16 calls), tensor-parallel: qkv_gate column-parallel + "
+                                   "NCCL all-gather, o row-parallel + NCCL all-reduce of FP32 partials",
+                       "l2": "cold by construction (>=250 MB of other weights between reuses of a matrix on one GPU "
+                             "at N=1; per-GPU shards at N>1)",
+                       "timing": ("CUDA-graph replay" if use_graph else "eager launches") +
+                                 " of the step, CUDA events, max over ranks",
+                       "parallelism": f"tp{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(value * 1e3 / world, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(value * 1e3 / world / hbm, 4), "traffic": None,
+                         "kernel": "whole step per GPU (GEMV + collectives)", "peak_kind": f"{peak_kind} hbm_gbs"},
+            "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+                    "h2d_bytes_per_step": sum(2 * c[4] * c[6] for c in calls),
+                    "d2h_bytes_per_step": sum(2 * c[4] * c[5] for c in calls), "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": 2 * len(calls) * args.steps,  # per call: the GEMV + the assemble / BF16-rounding kernel
+            "clocks": clocks,
+            "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    if g is not None:
+        del g
+    torch.cuda.synchronize()
+
+
 def run_profile(spec: str, launches: int = 3):
     """--profile LAYER:M:VARIANT -- a few launches of one call for an ncu capture (no timing, no output)."""
     import torch
@@ -361,6 +489,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif world > 1:
+            run_mbp_tp(args, rank, world)
         else:
             run_mbp(args, rank, world)
     finally:

@@ -138,6 +138,14 @@ int mbp_gemm_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t
 int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
                      cudaStream_t stream);
 
+/* ---- tensor-parallel helpers (no counterpart in the reference, which is single-GPU) ----
+ * Column-parallel: each rank computes a [m, ns] shard of out; an all-gather into one buffer yields [P][m][ns];
+ * mbp_tp_assemble_columns writes the row-major [m][P*ns] output (ns % 8 == 0).
+ * Row-parallel: each rank computes FP32 partial sums of the full output from its K slice; after the NCCL sum,
+ * mbp_f32_to_bf16 rounds them to the BF16 output (n % 4 == 0). */
+int mbp_tp_assemble_columns(const uint16_t* gathered, uint16_t* out, int P, int m, int ns, cudaStream_t stream);
+int mbp_f32_to_bf16(const float* in, uint16_t* out, long long n, cudaStream_t stream);
+
 /* ---- FP32 router through the hi/lo pair (replaces rr_launch / rr_scalar / rr_small S:856-861, routertail
  * S:5424, rwdl S:5377): out_f32[m, n] = x . hi^T + x . lo^T, FP32 accumulation. ---- */
 int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,

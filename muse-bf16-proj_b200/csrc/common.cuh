@@ -104,7 +104,7 @@ MBP_DEV void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32
       : "memory");
 }
 
-// 2-D tiled TMA load (no multicast) of box {x, y} from a tensor map in kernel-parameter space.
+// 2-D tiled TMA load of box {x, y} into this CTA's shared memory, from a tensor map in kernel-parameter space.
 MBP_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::

@@ -1,0 +1,140 @@
+"""Tensor-parallel host logic on CPU ranks (gloo, world size 2): the sharding plan, the collective choreography
+and the output assembly reproduce the unsharded projection; a rank that disappears makes the survivor's
+collective fail within the process-group timeout instead of hanging.  The local products are computed by the CPU
+oracle (each rank packs its own shard with its own exponent bases and escapes), so no GPU is involved."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import PKG_DIR, ROOT
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _bits(t):
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _setup(rank, world, port, timeout_s=60):
+    import sys
+    for p in (ROOT, PKG_DIR):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _worker_parity(rank, world, port, errq):
+    try:
+        _setup(rank, world, port)
+        from mbp.tp import TPPlan
+        from oracle import c12, oracle
+        g = torch.Generator().manual_seed(0)
+        n, k = 256, 512
+        w = (torch.randn(n, k, generator=g) * 0.02)
+        idx = torch.randperm(n * k, generator=torch.Generator().manual_seed(2))[: n * k // 100]
+        w.view(-1)[idx] *= 256
+        w = w.to(torch.bfloat16)
+        for m in (1, 5, 32):
+            x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+            full = torch.from_numpy(oracle.linear_f64(_bits(x), _bits(w))).float()
+            # column-parallel: shard rows, gather rank-major, assemble [m, n]
+            plan = TPPlan("column", world, rank, n, k)
+            pk = oracle.pack(_bits(plan.shard(w)), tile_base=True)
+            local, _ = oracle.gemv_packed(_bits(plan.x_slice(x)), pk)
+            parts = [torch.empty_like(torch.from_numpy(local)) for _ in range(world)]
+            dist.all_gather(parts, torch.from_numpy(local))
+            gathered = torch.stack(parts)                               # [P, m, n/P]
+            out = gathered.permute(1, 0, 2).reshape(m, n)
+            assert torch.allclose(out, full, rtol=1e-4, atol=1e-4), ("column", m)
+            # row-parallel: shard columns, FP32 partials, all-reduce; reduce-scatter keeps a column slice
+            plan = TPPlan("row", world, rank, n, k)
+            pk = oracle.pack(_bits(plan.shard(w)), tile_base=True)
+            part, _ = oracle.gemv_packed(_bits(plan.x_slice(x)), pk)
+            part = torch.from_numpy(part)
+            red = part.clone()
+            dist.all_reduce(red)
+            assert torch.allclose(red, full, rtol=1e-4, atol=1e-4), ("row", m)
+            c0, c1 = plan.scatter_cols()
+            assert torch.allclose(red[:, c0:c1], full[:, rank * n // world:(rank + 1) * n // world], rtol=1e-4,
+                                  atol=1e-4), ("scatter", m)
+            # every rank's shard round-trips through the per-shard packing exactly
+            assert np.array_equal(oracle.unpack(pk), _bits(plan.shard(w)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+def test_tp_plan_parity_gloo():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    procs = [ctx.Process(target=_worker_parity, args=(r, world, port, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert all(p.exitcode == 0 for p in procs), errs
+
+
+def _worker_missing(rank, world, port, q):
+    _setup(rank, world, port, timeout_s=5)
+    if rank == 1:
+        os._exit(3)  # leaves between steps, with no collective in flight
+    t = torch.ones(4)
+    try:
+        dist.all_reduce(t)
+        q.put("rank0-no-error")
+    except Exception as e:
+        q.put(f"rank0-error:{type(e).__name__}")
+
+
+def test_tp_missing_rank_times_out():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker_missing, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    msgs = []
+    while not q.empty():
+        msgs.append(q.get())
+    assert procs[1].exitcode == 3
+    assert any(m.startswith("rank0-error") for m in msgs), msgs
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+
+
+def test_plan_rules():
+    from mbp.tp import TPPlan
+    p = TPPlan("column", 4, 2, 14336, 6144)
+    assert p.rows == (7168, 10752) and p.cols == (0, 6144)
+    q = TPPlan("row", 8, 7, 6144, 6144)
+    assert q.cols == (5376, 6144) and q.rows == (0, 6144) and q.scatter_cols() == (5376, 6144)
+    with pytest.raises(ValueError):
+        TPPlan("row", 8, 0, 6144, 6000)
+    with pytest.raises(ValueError):
+        TPPlan("column", 3, 0, 6144 + 16, 6144)
