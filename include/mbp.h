@@ -81,6 +81,7 @@ typedef struct mbp_gemv_geom {
   int32_t wki;     /* consumer warps splitting a CTA's K range */
   int32_t kci;     /* 64-column chunks per consumer warp per pipeline stage */
   int32_t stages;  /* pipeline depth */
+  int32_t nblk;    /* CTAs along the rows, tiles split evenly (at most rb each); 0 = ceil(n_out/16 / rb) */
 } mbp_gemv_geom;
 
 /* ---- library / device ---- */

@@ -52,6 +52,7 @@ struct __align__(64) GemvParams {
   int m;     // tokens
   int ldo;   // leading dimension of out (elements)
   int rb, split, wki, kci, stages;
+  int nblk;  // row blocks: block b owns row tiles [b*Rout/nblk, (b+1)*Rout/nblk), at most rb of them
 };
 
 struct Layout {
@@ -85,10 +86,13 @@ inline int smem_request(const Layout& L) { return L.total + 1024; }  // + alignm
 
 // Chunks per unrolled consumer pass and independent accumulators per (row tile, token tile), sized so that a
 // pass's unit loads, B fragments and accumulators fit in 128 registers without spills.
-__host__ __device__ constexpr int kc_for(int fmt, int mt) {
-  return fmt == FMT_C12 ? (mt == 1 ? 4 : mt == 2 ? 2 : 1) : (mt == 1 ? 2 : 1);
+__host__ __device__ constexpr int kc_for(int fmt, int mt, int rtw) {
+  return rtw == 2 ? (fmt == FMT_C12 && mt == 1 ? 2 : 1)
+                  : fmt == FMT_C12 ? (mt == 1 ? 4 : mt == 2 ? 2 : 1) : (mt == 1 ? 2 : 1);
 }
-__host__ __device__ constexpr int na_for(int fmt, int mt) { return mt == 4 ? 1 : 2 + 2 * (fmt == FMT_C12 && mt == 1); }
+__host__ __device__ constexpr int na_for(int fmt, int mt, int rtw) {
+  return rtw == 2 ? (mt == 1 ? 2 : 1) : mt == 4 ? 1 : 2 + 2 * (fmt == FMT_C12 && mt == 1);
+}
 
 template <int FMT>
 struct Fmt;
@@ -109,8 +113,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   using OutT = typename std::conditional<F32OUT, float, uint16_t>::type;
   constexpr int UB = Fmt<FMT>::UB;
   constexpr int TOK = 8 * MT;
-  constexpr int KC = kc_for(FMT, MT);  // chunks per unrolled pass
-  constexpr int NA = na_for(FMT, MT);  // independent accumulators per (row tile, token tile)
+  constexpr int KC = kc_for(FMT, MT, RTW);  // chunks per unrolled pass
+  constexpr int NA = na_for(FMT, MT, RTW);  // independent accumulators per (row tile, token tile)
   constexpr int NL = FMT == FMT_C12 ? 3 : 8;         // 16-byte loads per lane per unit
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -122,8 +126,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   unsigned char* smem = smem_raw + (sbase - raw_base);
   const uint32_t full0 = sbase + L.bar_off, empty0 = full0 + 8 * p.stages;
 
-  const int r0 = blockIdx.x * p.rb;
-  const int rvalid = min(p.rb, p.Rout - r0);
+  const int r0 = (int)((long long)blockIdx.x * p.Rout / p.nblk);
+  const int rvalid = (int)((long long)(blockIdx.x + 1) * p.Rout / p.nblk) - r0;  // <= rb
   const int tok0 = blockIdx.z * TOK;
   const int s = blockIdx.y;
   const int cs = (int)((long long)s * p.C / p.split), ce = (int)((long long)(s + 1) * p.C / p.split);
@@ -373,10 +377,12 @@ KernelFn kernel_ptr() {
   return reinterpret_cast<KernelFn>(&k_gemv<FMT, MT, RTW, F32>);
 }
 
-KernelFn pick(int fmt, int mt, bool f32) {
+KernelFn pick(int fmt, int mt, int rtw, bool f32) {
   if (fmt == FMT_C12) {
-    if (mt == 1) return f32 ? kernel_ptr<FMT_C12, 1, 1, true>() : kernel_ptr<FMT_C12, 1, 1, false>();
-    if (mt == 2) return f32 ? kernel_ptr<FMT_C12, 2, 1, true>() : kernel_ptr<FMT_C12, 2, 1, false>();
+    if (mt == 1 && rtw == 1) return f32 ? kernel_ptr<FMT_C12, 1, 1, true>() : kernel_ptr<FMT_C12, 1, 1, false>();
+    if (mt == 1) return f32 ? kernel_ptr<FMT_C12, 1, 2, true>() : kernel_ptr<FMT_C12, 1, 2, false>();
+    if (mt == 2 && rtw == 1) return f32 ? kernel_ptr<FMT_C12, 2, 1, true>() : kernel_ptr<FMT_C12, 2, 1, false>();
+    if (mt == 2) return f32 ? kernel_ptr<FMT_C12, 2, 2, true>() : kernel_ptr<FMT_C12, 2, 2, false>();
     return f32 ? kernel_ptr<FMT_C12, 4, 2, true>() : kernel_ptr<FMT_C12, 4, 2, false>();
   }
   if (mt == 1) return kernel_ptr<FMT_HILO, 1, 1, true>();
@@ -386,6 +392,8 @@ KernelFn pick(int fmt, int mt, bool f32) {
 
 int mt_of(int m) { return m <= 8 ? 1 : m <= 16 ? 2 : 4; }
 int rtw_of(int mt) { return mt == 4 ? 2 : 1; }
+// register-tile widths that have an instance for this format and token tile
+bool rtw_ok(int fmt, int mt, int rtw) { return rtw == 2 ? (fmt == FMT_C12 || mt == 4) : mt != 4; }
 int ub_of(int fmt) { return fmt == FMT_C12 ? MBP_C12_UNIT_BYTES : 2 * MBP_RAW_UNIT_BYTES; }
 
 // Per-device one-time function attributes (max dynamic shared memory, non-portable cluster sizes).
@@ -469,15 +477,17 @@ int max_ctas(KernelFn fn, int split, int threads, int smem) {
 int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
   constexpr double kHbmBw = 6.0e12, kSmBw = 45.0e9, kSplitCost = 1.2e-6;
   const int ub = ub_of(fmt);
-  const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt, kc = kc_for(fmt, mt);
+  const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt, kc = kc_for(fmt, mt, rtw);
   const int zb = (m + tok - 1) / tok;
-  const KernelFn fn = pick(fmt, mt, f32);
+  const KernelFn fn = pick(fmt, mt, rtw, f32);
   const int sms = sm_count();
   const double total = (double)Rout * C * ub * zb;
   double best = 1e30;
   mbp_gemv_geom bg = {};
   const int rb_max = ((Rout + rtw - 1) / rtw) * rtw;
-  for (int split = 1; split <= 16 && split <= C; ++split) {
+  // cluster sizes that pack evenly into the GPCs (sizes like 5 or 7 strand SMs and measured far slower)
+  for (const int split : {1, 2, 3, 4, 6, 8}) {
+    if (split > C) break;
     const int cpc = (C + split - 1) / split;
     for (int rb = rtw; rb <= kMaxConsumerWarps * rtw && rb <= rb_max; rb += rtw) {
       const int rows_w = rb / rtw;
@@ -520,6 +530,7 @@ int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
         bg.wki = wki;
         bg.kci = kci;
         bg.stages = st;
+        bg.nblk = nblk;
       }
     }
   }
@@ -561,7 +572,7 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   if (n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
   if (ldo < n_out) return MBP_ERR_SHAPE;
   if (((uintptr_t)x & 15u) || ((uintptr_t)units & 15u)) return MBP_ERR_ALIGN;
-  const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt, kc = kc_for(fmt, mt);
+  const int mt = mt_of(m), tok = 8 * mt;
   const int Rout = n_out / 16;
   mbp_gemv_geom g;
   if (geom) {
@@ -570,15 +581,18 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
     const int rc = plan_impl(fmt, Rout, C, m, f32, &g);
     if (rc) return rc;
   }
-  if (g.rtw != rtw || g.rb < rtw || g.rb % rtw || g.rb / rtw > kMaxConsumerWarps) return MBP_ERR_SPLIT;
+  const int rtw = g.rtw, kc = kc_for(fmt, mt, rtw);
+  if (!rtw_ok(fmt, mt, rtw) || g.rb < rtw || g.rb % rtw || g.rb / rtw > kMaxConsumerWarps) return MBP_ERR_SPLIT;
   if (g.split < 1 || g.split > 16 || g.split > C || g.wki < 1 || g.kci < kc || g.kci % kc || g.stages < 1)
     return MBP_ERR_SPLIT;
   const int rows_w = g.rb / rtw;
   if (rows_w * g.wki > kMaxConsumerWarps) return MBP_ERR_SPLIT;
+  const int nblk = g.nblk > 0 ? g.nblk : (Rout + g.rb - 1) / g.rb;
+  if (nblk > Rout || (Rout + nblk - 1) / nblk > g.rb) return MBP_ERR_SPLIT;  // a block holds at most rb tiles
   const int ub = ub_of(fmt);
   const Layout L = make_layout(ub, mt, g.rb, rtw, g.wki, g.kci, g.stages, fmt == FMT_C12);
   if (smem_request(L) > kMaxSmem) return MBP_ERR_SMEM;
-  const KernelFn fn = pick(fmt, mt, f32);
+  const KernelFn fn = pick(fmt, mt, rtw, f32);
   int rc = ensure_attrs(fn);
   if (rc) return rc;
   GemvParams p;
@@ -599,8 +613,9 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   p.wki = g.wki;
   p.kci = g.kci;
   p.stages = g.stages;
+  p.nblk = nblk;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((Rout + g.rb - 1) / g.rb, g.split, (m + tok - 1) / tok);
+  cfg.gridDim = dim3(nblk, g.split, (m + tok - 1) / tok);
   cfg.blockDim = dim3(32 * (rows_w * g.wki + 1));
   cfg.dynamicSmemBytes = smem_request(L);
   cfg.stream = stream;

@@ -40,10 +40,11 @@ class HiLo(ctypes.Structure):
 
 class Geom(ctypes.Structure):
     _fields_ = [("rb", ctypes.c_int32), ("rtw", ctypes.c_int32), ("split", ctypes.c_int32),
-                ("wki", ctypes.c_int32), ("kci", ctypes.c_int32), ("stages", ctypes.c_int32)]
+                ("wki", ctypes.c_int32), ("kci", ctypes.c_int32), ("stages", ctypes.c_int32),
+                ("nblk", ctypes.c_int32)]
 
     def as_tuple(self):
-        return (self.rb, self.rtw, self.split, self.wki, self.kci, self.stages)
+        return (self.rb, self.rtw, self.split, self.wki, self.kci, self.stages, self.nblk)
 
 
 # (name, restype, argtypes) for every symbol of include/mbp.h

@@ -134,7 +134,8 @@ def test_explicit_geometries_agree():
     x = tokens(8, 3072, seed=1)
     ref = mbp.gemv(p, x, out_dtype=torch.float32)
     for g in [Geom(8, 1, 1, 1, 4, 2), Geom(4, 1, 3, 2, 4, 3), Geom(2, 1, 8, 4, 4, 2), Geom(1, 1, 6, 3, 4, 2),
-              Geom(11, 1, 2, 1, 4, 2), Geom(3, 1, 1, 2, 8, 2)]:
+              Geom(11, 1, 2, 1, 4, 2), Geom(3, 1, 1, 2, 8, 2), Geom(3, 1, 1, 2, 4, 2, 23),
+              Geom(8, 1, 2, 1, 4, 2, 9)]:
         out = mbp.gemv(p, x, out_dtype=torch.float32, geom=g)
         # same FP32 products, different split-K summation order
         assert torch.allclose(out, ref, rtol=1e-4, atol=1e-3), g.as_tuple()
