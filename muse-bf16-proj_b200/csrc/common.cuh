@@ -223,6 +223,28 @@ MBP_DEV void decode_unit(const uint4& p0, const uint4& p1, const uint4& p2, uint
   decode8(p1.z, p1.w, p2.w, T0, T1, A + 12);
 }
 
+// decode8 with escape restoration: X0/X1 hold the exponent XOR bytes of values 0-3 / 4-7 (the byte order of the
+// table lookups h0/h1), applied to the high bytes before the sign is merged.
+MBP_DEV void decode8m(uint32_t L0, uint32_t L1, uint32_t C, uint32_t T0, uint32_t T1, uint32_t X0, uint32_t X1,
+                      uint32_t* a) {
+  const uint32_t cm = C & 0x77777777u;
+  const uint32_t h0 = prmt(T0, T1, cm) ^ X0;
+  const uint32_t h1 = prmt(T0, T1, cm >> 16) ^ X1;
+  a[0] = prmt(L0, h0, 0x5140u) | ((C << 12) & 0x80008000u);
+  a[1] = prmt(L0, h0, 0x7362u) | ((C << 8) & 0x80008000u);
+  a[2] = prmt(L1, h1, 0x5140u) | ((C << 4) & 0x80008000u);
+  a[3] = prmt(L1, h1, 0x7362u) | (C & 0x80008000u);
+}
+
+// decode_unit with the lane's two unit-mask words (m0 = values 0-15, m1 = values 16-31, one byte per value).
+MBP_DEV void decode_unit_m(const uint4& p0, const uint4& p1, const uint4& p2, uint32_t T0, uint32_t T1,
+                           const uint4& m0, const uint4& m1, uint32_t (&A)[16]) {
+  decode8m(p0.x, p0.y, p2.x, T0, T1, m0.x, m0.y, A + 0);
+  decode8m(p0.z, p0.w, p2.y, T0, T1, m0.z, m0.w, A + 4);
+  decode8m(p1.x, p1.y, p2.z, T0, T1, m1.x, m1.y, A + 8);
+  decode8m(p1.z, p1.w, p2.w, T0, T1, m1.z, m1.w, A + 12);
+}
+
 MBP_DEV uint32_t table_lo(uint32_t base) { return base * 0x01010101u + 0x03020100u; }
 MBP_DEV uint32_t table_hi(uint32_t base) { return base * 0x01010101u + 0x07060504u; }
 
@@ -230,6 +252,5 @@ MBP_DEV uint32_t table_hi(uint32_t base) { return base * 0x01010101u + 0x0706050
 MBP_DEV uint32_t esc_chunk(uint32_t e) { return e >> 17; }
 MBP_DEV uint32_t esc_lane(uint32_t e) { return (e >> 12) & 31u; }
 MBP_DEV uint32_t esc_value(uint32_t e) { return (e >> 7) & 31u; }
-MBP_DEV uint32_t esc_xor_word(uint32_t e) { return (e & 0x7Fu) << (8 + 16 * ((e >> 7) & 1u)); }
 
 }  // namespace mbp

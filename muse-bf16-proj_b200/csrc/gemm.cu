@@ -66,7 +66,7 @@ __host__ __device__ inline GLayout gemm_layout(int bn) {
   L.a = L.packed + kPS * kPackedStage;  // multiple of 1024
   L.x = L.a + kAS * kAStage;            // multiple of 1024
   L.xr = L.x + kXS * bn * 128;          // bn multiple of 16 -> multiple of 2048
-  L.bars = L.xr + kDecWarps * kXorWarpBytes;
+  L.bars = L.xr + kDecWarps * kMaskUnitBytes;
   L.tmem_slot = L.bars + 8 * (2 * kPS + 2 * kAS + 2 * kXS + 1);
   L.total = L.tmem_slot + 16;
   return L;
@@ -216,8 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     const bool valid = rt < p.Rout;
     uint32_t T0 = 0, T1 = 0;
     EscCursor cur;
-    const uint32_t xr = base + L.xr + dw * kXorWarpBytes;
-    xor_mask_clear(xr, lane);
+    const uint32_t xr = base + L.xr + dw * kMaskUnitBytes;
+    mask_clear(xr, kMaskUnitBytes, lane);
     if (valid) {
       const uint32_t b = p.bases[rt];
       T0 = table_lo(b);
@@ -245,10 +245,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       const uint4 p2 = *reinterpret_cast<const uint4*>(u + 1024);
       mbar_arrive(pempty + 8 * ps);
       uint32_t A[16];
-      decode_unit(p0, p1, p2, T0, T1, A);
-      if (valid) {
-        cur.seek((uint32_t)(cs + i), lane);
-        cur.apply((uint32_t)(cs + i), A, xr, lane);
+      const uint32_t c = (uint32_t)(cs + i);
+      if (valid) cur.seek(c, lane);
+      if (valid && cur.next_chunk == c) {
+        uint32_t tgt[1] = {0u};
+        cur.scatter<1>(c, c + 1, xr, kMaskUnitBytes, lane, tgt);
+        __syncwarp();
+        uint4 m0, m1;
+        take_mask(xr, tgt[0], lane, m0, m1);
+        decode_unit_m(p0, p1, p2, T0, T1, m0, m1, A);
+      } else {
+        decode_unit(p0, p1, p2, T0, T1, A);
       }
       if (i >= kAS && !mbar_wait(aempty + 8 * as, ((i / kAS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
       unsigned char* a = sm + L.a + as * kAStage;

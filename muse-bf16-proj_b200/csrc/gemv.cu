@@ -52,37 +52,9 @@ struct __align__(64) GemvParams {
   int m;     // tokens
   int ldo;   // leading dimension of out (elements)
   int rb, split, wki, kci, stages;
-  int nblk;  // row blocks: block b owns row tiles [b*Rout/nblk, (b+1)*Rout/nblk), at most rb of them
+  int nblk;     // row blocks: block b owns row tiles [b*Rout/nblk, (b+1)*Rout/nblk), at most rb of them
+  int has_esc;  // the matrix has escapes: consumer warps get escape masks
 };
-
-struct Layout {
-  int xplane;   // bytes of one staged x chunk: 8*MT rows x 128 bytes
-  int xbytes;   // x bytes per stage
-  int sbytes;   // stage bytes (multiple of 1024)
-  int ring;     // ring bytes (also holds the split-K reduction after the main loop)
-  int xr_off;   // per-warp escape XOR masks
-  int bar_off;  // full[stages], empty[stages]
-  int total;    // bytes from the 1024-aligned base
-};
-
-__host__ __device__ inline Layout make_layout(int ub, int mt, int rb, int rtw, int wki, int kci, int stages,
-                                              bool c12) {
-  Layout L;
-  L.xplane = 8 * mt * 128;
-  L.xbytes = wki * kci * L.xplane;
-  const int wbytes = rb * wki * kci * ub;
-  L.sbytes = (L.xbytes + wbytes + 1023) & ~1023;
-  int ring = stages * L.sbytes;
-  const int red = (wki + 1) * rb * mt * 32 * 16;
-  if (red > ring) ring = red;
-  L.ring = (ring + 127) & ~127;
-  L.xr_off = L.ring;
-  L.bar_off = L.xr_off + (c12 ? (rb / rtw) * wki * kXorWarpBytes : 0);
-  L.total = L.bar_off + 2 * stages * 8;
-  return L;
-}
-
-inline int smem_request(const Layout& L) { return L.total + 1024; }  // + alignment slack
 
 // Chunks per unrolled consumer pass and independent accumulators per (row tile, token tile), sized so that a
 // pass's unit loads, B fragments and accumulators fit in 128 registers without spills.
@@ -93,6 +65,38 @@ __host__ __device__ constexpr int kc_for(int fmt, int mt, int rtw) {
 __host__ __device__ constexpr int na_for(int fmt, int mt, int rtw) {
   return rtw == 2 ? (mt == 1 ? 2 : 1) : mt == 4 ? 1 : 2 + 2 * (fmt == FMT_C12 && mt == 1);
 }
+
+struct Layout {
+  int xplane;   // bytes of one staged x chunk: 8*MT rows x 128 bytes
+  int xbytes;   // x bytes per stage
+  int sbytes;   // stage bytes (multiple of 1024)
+  int ring;     // ring bytes (also holds the split-K reduction after the main loop)
+  int mask;     // escape mask bytes per consumer warp: one 1 KB unit mask per unit of a pass (0 without escapes)
+  int xr_off;   // per-warp escape masks
+  int bar_off;  // full[stages], empty[stages]
+  int total;    // bytes from the 1024-aligned base
+};
+
+__host__ __device__ inline Layout make_layout(int fmt, int mt, int rb, int rtw, int wki, int kci, int stages,
+                                              bool esc) {
+  const int ub = fmt == FMT_C12 ? MBP_C12_UNIT_BYTES : 2 * MBP_RAW_UNIT_BYTES;
+  Layout L;
+  L.xplane = 8 * mt * 128;
+  L.xbytes = wki * kci * L.xplane;
+  const int wbytes = rb * wki * kci * ub;
+  L.sbytes = (L.xbytes + wbytes + 1023) & ~1023;
+  int ring = stages * L.sbytes;
+  const int red = (wki + 1) * rb * mt * 32 * 16;
+  if (red > ring) ring = red;
+  L.ring = (ring + 127) & ~127;
+  L.mask = (fmt == FMT_C12 && esc) ? kc_for(fmt, mt, rtw) * rtw * kMaskUnitBytes : 0;
+  L.xr_off = L.ring;
+  L.bar_off = L.xr_off + (rb / rtw) * wki * L.mask;
+  L.total = L.bar_off + 2 * stages * 8;
+  return L;
+}
+
+inline int smem_request(const Layout& L) { return L.total + 1024; }  // + alignment slack
 
 template <int FMT>
 struct Fmt;
@@ -120,7 +124,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int rows_w = p.rb / RTW;
   const int nwc = rows_w * p.wki;
-  const Layout L = make_layout(UB, MT, p.rb, RTW, p.wki, p.kci, p.stages, FMT == FMT_C12);
+  const Layout L = make_layout(FMT, MT, p.rb, RTW, p.wki, p.kci, p.stages, p.has_esc != 0);
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t sbase = (raw_base + 1023u) & ~1023u;
   unsigned char* smem = smem_raw + (sbase - raw_base);
@@ -188,23 +192,27 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   } else {
     // ---------------- consumers ----------------
     const int b = cs + wk * Lk, e = min(cs + (wk + 1) * Lk, ce);
+    bool rvalid_j[RTW];
+#pragma unroll
+    for (int j = 0; j < RTW; ++j) rvalid_j[j] = wr * RTW + j < rvalid;
     uint32_t T0[RTW], T1[RTW];
     EscCursor cur[RTW];
-    const uint32_t xr = sbase + L.xr_off + warp * kXorWarpBytes;
+    const uint32_t xr = sbase + L.xr_off + warp * L.mask;  // unit mask of (chunk jc, tile j): xr + (jc*RTW + j) KB
     if constexpr (FMT == FMT_C12) {
-      xor_mask_clear(xr, lane);
+      if (L.mask) mask_clear(xr, L.mask, lane);
 #pragma unroll
       for (int j = 0; j < RTW; ++j) {
         const int rt = r0 + wr * RTW + j;
         T0[j] = T1[j] = 0;
-        if (rt < p.Rout && b < e) {
+        if (rvalid_j[j] && b < e) {
           const uint32_t base = p.bases[rt];
           T0[j] = table_lo(base);
           T1[j] = table_hi(base);
-          cur[j].init(p.esc, p.esc_off[(size_t)rt * p.C + b], p.esc_off[(size_t)rt * p.C + e], lane);
-        } else {
-          cur[j].init(p.esc, 0, 0, lane);
         }
+        if (rvalid_j[j] && b < e && p.has_esc)
+          cur[j].init(p.esc, p.esc_off[(size_t)rt * p.C + b], p.esc_off[(size_t)rt * p.C + e], lane);
+        else
+          cur[j].init(p.esc, 0, 0, lane);
       }
     }
     const int g = lane >> 2, t = lane & 3;
@@ -215,14 +223,27 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
       uoff[j] = (uint32_t)L.xbytes + (uint32_t)((min(wr * RTW + j, p.rb - 1) * p.wki + wk) * p.kci) * UB + lane * 16;
     const uint32_t xoff = (uint32_t)(wk * p.kci * L.xplane + g * 128);
     const uint32_t swz0 = ((2 * t) ^ g) << 4, swz1 = ((2 * t + 1) ^ g) << 4;
-    bool rvalid_j[RTW];
-#pragma unroll
-    for (int j = 0; j < RTW; ++j) rvalid_j[j] = wr * RTW + j < rvalid;
 
-    // One pass of KC chunks.  ESC selects the variant that patches escapes; a stage whose chunk range holds
-    // none of this warp's escapes runs the variant without any escape code.
-    auto pass_fn = [&](const unsigned char* stage, int c0, int cl0, int nk, auto esc_tag) {
+    // One pass of KC chunks [c0 + cl0, c0 + min(cl0 + KC, nk)).  ESC selects the variant that restores
+    // escapes (one mask scatter and one __syncwarp for the whole pass); a pass whose chunks hold none of this
+    // warp's escapes runs the variant without any escape code.  FULL passes (all KC chunks present, the common
+    // case) are straight-line code, so the compiler interleaves the decode of one unit with the mma of another.
+    // A second tile past the block's valid rows (RTW = 2) is decoded from zero tables and never stored.
+    auto pass_fn = [&](const unsigned char* stage, int c0, int cl0, int nk, auto esc_tag, auto full_tag) {
       constexpr bool ESC = decltype(esc_tag)::value;
+      constexpr bool FULL = decltype(full_tag)::value;
+      uint32_t tgt[RTW][KC];  // lanes holding escape bytes, per (tile, chunk) of the pass
+      if constexpr (ESC) {
+        const uint32_t cb = (uint32_t)(c0 + cl0), cend = (uint32_t)(c0 + min(cl0 + KC, nk));
+#pragma unroll
+        for (int j = 0; j < RTW; ++j) {
+#pragma unroll
+          for (int jc = 0; jc < KC; ++jc) tgt[j][jc] = 0u;
+          if (cur[j].next_chunk < cend)
+            cur[j].scatter<KC>(cb, cend, xr + (uint32_t)j * kMaskUnitBytes, RTW * kMaskUnitBytes, lane, tgt[j]);
+        }
+        __syncwarp();
+      }
       uint4 u[KC][RTW][NL];  // all units of the pass first: independent shared loads in flight together
 #pragma unroll
       for (int jc = 0; jc < KC; ++jc)
@@ -232,10 +253,20 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
 #pragma unroll
           for (int l = 0; l < NL; ++l) u[jc][j][l] = src[l * 32];
         }
+      uint4 mk[ESC ? KC : 1][RTW][2];
+      if constexpr (ESC) {
+#pragma unroll
+        for (int jc = 0; jc < KC; ++jc)
+#pragma unroll
+          for (int j = 0; j < RTW; ++j)
+            take_mask(xr + (uint32_t)(jc * RTW + j) * kMaskUnitBytes, tgt[j][jc], lane, mk[jc][j][0], mk[jc][j][1]);
+      }
 #pragma unroll
       for (int jc = 0; jc < KC; ++jc) {
         const int cl = cl0 + jc;  // chunk within the stage
-        if (cl >= nk) break;
+        if constexpr (!FULL) {
+          if (cl >= nk) break;
+        }
         const unsigned char* xrow = stage + xoff + cl * L.xplane;
         uint32_t bx[MT][8];
 #pragma unroll
@@ -247,11 +278,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
         }
 #pragma unroll
         for (int j = 0; j < RTW; ++j) {
-          if (!rvalid_j[j]) continue;
           uint32_t A[16];
           if constexpr (FMT == FMT_C12) {
-            decode_unit(u[jc][j][0], u[jc][j][1], u[jc][j][2], T0[j], T1[j], A);
-            if constexpr (ESC) cur[j].apply((uint32_t)(c0 + cl), A, xr, lane);
+            if constexpr (ESC)
+              decode_unit_m(u[jc][j][0], u[jc][j][1], u[jc][j][2], T0[j], T1[j], mk[jc][j][0], mk[jc][j][1], A);
+            else
+              decode_unit(u[jc][j][0], u[jc][j][1], u[jc][j][2], T0[j], T1[j], A);
 #pragma unroll
             for (int n = 0; n < MT; ++n)
 #pragma unroll
@@ -284,16 +316,27 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
       if (!mbar_wait(full0 + 8 * st, ph, MBP_DEV_TIMEOUT_FULL)) break;
       const unsigned char* stage = smem + st * L.sbytes;
       const int c0 = b + it * p.kci;
-      const int nk = max(0, min(p.kci, e - c0));
-      bool esc_here = false;
-      if constexpr (FMT == FMT_C12) {
+      const int nk = rvalid_j[0] ? max(0, min(p.kci, e - c0)) : 0;  // a warp without valid rows only drains
+      for (int cl0 = 0; cl0 < nk; cl0 += KC) {
+        const bool full = cl0 + KC <= nk;
+        bool esc_here = false;
+        if constexpr (FMT == FMT_C12) {
 #pragma unroll
-        for (int j = 0; j < RTW; ++j) esc_here |= (int)cur[j].next_chunk < c0 + nk;
-      }
-      if (esc_here) {
-        for (int cl0 = 0; cl0 < nk; cl0 += KC) pass_fn(stage, c0, cl0, nk, std::true_type{});
-      } else {
-        for (int cl0 = 0; cl0 < nk; cl0 += KC) pass_fn(stage, c0, cl0, nk, std::false_type{});
+          for (int j = 0; j < RTW; ++j) esc_here |= (int)cur[j].next_chunk < c0 + min(cl0 + KC, nk);
+        }
+        if constexpr (FMT == FMT_C12) {
+          if (esc_here) {
+            if (full)
+              pass_fn(stage, c0, cl0, nk, std::true_type{}, std::true_type{});
+            else
+              pass_fn(stage, c0, cl0, nk, std::true_type{}, std::false_type{});
+            continue;
+          }
+        }
+        if (full)
+          pass_fn(stage, c0, cl0, nk, std::false_type{}, std::true_type{});
+        else
+          pass_fn(stage, c0, cl0, nk, std::false_type{}, std::false_type{});
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * st);
@@ -474,7 +517,7 @@ int max_ctas(KernelFn fn, int split, int threads, int smem) {
 //   * each level of cluster split-K costs a fixed reduction / synchronisation overhead;
 //   * ~8 consumer warps per SM (fewer, fatter CTAs when the token tile is large and 2 CTAs fit an SM).
 // Only single-wave launches are considered.
-int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
+int plan_search(int fmt, int Rout, int C, int m, bool f32, bool esc, mbp_gemv_geom* g) {
   constexpr double kHbmBw = 6.0e12, kSmBw = 45.0e9, kSplitCost = 1.2e-6;
   const int ub = ub_of(fmt);
   const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt, kc = kc_for(fmt, mt, rtw);
@@ -505,9 +548,9 @@ int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
       const int slot_w = rb * wki * kci * ub;
       int st = 2;
       while (st < 4 && (st + 1) * slot_w <= 192 * 1024 &&
-             smem_request(make_layout(ub, mt, rb, rtw, wki, kci, st + 1, fmt == FMT_C12)) <= kMaxSmem)
+             smem_request(make_layout(fmt, mt, rb, rtw, wki, kci, st + 1, esc)) <= kMaxSmem)
         ++st;
-      const Layout L = make_layout(ub, mt, rb, rtw, wki, kci, st, fmt == FMT_C12);
+      const Layout L = make_layout(fmt, mt, rb, rtw, wki, kci, st, esc);
       if (smem_request(L) > kMaxSmem) continue;
       const int threads = 32 * (rows_w * wki + 1);
       const int cap = max_ctas(fn, split, threads, smem_request(L));
@@ -540,15 +583,15 @@ int plan_search(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
 }
 
 std::mutex g_plan_mu;
-std::map<std::tuple<int, int, int, int, int, int, bool>, mbp_gemv_geom> g_plans;
+std::map<std::tuple<int, int, int, int, int, int, bool, bool>, mbp_gemv_geom> g_plans;
 
 // Planned geometries are cached per (device, format, shape, token tile count, output type).
-int plan_impl(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
+int plan_impl(int fmt, int Rout, int C, int m, bool f32, bool esc, mbp_gemv_geom* g) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int mt = mt_of(m);
   const int zb = (m + 8 * mt - 1) / (8 * mt);
-  const auto key = std::make_tuple(dev, fmt, Rout, C, mt, zb, f32);
+  const auto key = std::make_tuple(dev, fmt, Rout, C, mt, zb, f32, esc);
   {
     std::lock_guard<std::mutex> lk(g_plan_mu);
     auto it = g_plans.find(key);
@@ -557,7 +600,7 @@ int plan_impl(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
       return MBP_OK;
     }
   }
-  const int rc = plan_search(fmt, Rout, C, m, f32, g);
+  const int rc = plan_search(fmt, Rout, C, m, f32, esc, g);
   if (rc == MBP_OK) {
     std::lock_guard<std::mutex> lk(g_plan_mu);
     g_plans[key] = *g;
@@ -566,19 +609,20 @@ int plan_impl(int fmt, int Rout, int C, int m, bool f32, mbp_gemv_geom* g) {
 }
 
 int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* esc_off, const uint32_t* esc,
-           int C, int K, int n_out, const uint16_t* x, int m, void* out, int ldo, bool f32, const mbp_gemv_geom* geom,
-           cudaStream_t stream) {
+           int64_t n_esc, int C, int K, int n_out, const uint16_t* x, int m, void* out, int ldo, bool f32,
+           const mbp_gemv_geom* geom, cudaStream_t stream) {
   if (m < 1) return MBP_ERR_M;
   if (n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
   if (ldo < n_out) return MBP_ERR_SHAPE;
   if (((uintptr_t)x & 15u) || ((uintptr_t)units & 15u)) return MBP_ERR_ALIGN;
   const int mt = mt_of(m), tok = 8 * mt;
   const int Rout = n_out / 16;
+  const bool with_esc = fmt == FMT_C12 && n_esc > 0;
   mbp_gemv_geom g;
   if (geom) {
     g = *geom;
   } else {
-    const int rc = plan_impl(fmt, Rout, C, m, f32, &g);
+    const int rc = plan_impl(fmt, Rout, C, m, f32, with_esc, &g);
     if (rc) return rc;
   }
   const int rtw = g.rtw, kc = kc_for(fmt, mt, rtw);
@@ -589,8 +633,7 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   if (rows_w * g.wki > kMaxConsumerWarps) return MBP_ERR_SPLIT;
   const int nblk = g.nblk > 0 ? g.nblk : (Rout + g.rb - 1) / g.rb;
   if (nblk > Rout || (Rout + nblk - 1) / nblk > g.rb) return MBP_ERR_SPLIT;  // a block holds at most rb tiles
-  const int ub = ub_of(fmt);
-  const Layout L = make_layout(ub, mt, g.rb, rtw, g.wki, g.kci, g.stages, fmt == FMT_C12);
+  const Layout L = make_layout(fmt, mt, g.rb, rtw, g.wki, g.kci, g.stages, with_esc);
   if (smem_request(L) > kMaxSmem) return MBP_ERR_SMEM;
   const KernelFn fn = pick(fmt, mt, rtw, f32);
   int rc = ensure_attrs(fn);
@@ -614,6 +657,7 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   p.kci = g.kci;
   p.stages = g.stages;
   p.nblk = nblk;
+  p.has_esc = with_esc ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nblk, g.split, (m + tok - 1) / tok);
   cfg.blockDim = dim3(32 * (rows_w * g.wki + 1));
@@ -641,7 +685,7 @@ int mbp_gemv_plan(int n_out, int k, int m, mbp_gemv_geom* geom) {
   if (!geom) return MBP_ERR_ARG;
   if (n_out <= 0 || n_out % 16 || k <= 0 || k % 64) return MBP_ERR_SHAPE;
   if (m < 1) return MBP_ERR_M;
-  return plan_impl(FMT_C12, n_out / 16, k / 64, m, false, geom);
+  return plan_impl(FMT_C12, n_out / 16, k / 64, m, false, true, geom);
 }
 
 int mbp_gemv_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo,
@@ -649,8 +693,8 @@ int mbp_gemv_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t
   if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
   if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n) return MBP_ERR_SHAPE;
-  return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, w->k / 64, w->k, n_out, x, m, out, ldo, false, geom,
-                stream);
+  return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, w->n_esc, w->k / 64, w->k, n_out, x, m, out, ldo,
+                false, geom, stream);
 }
 
 int mbp_gemv_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
@@ -658,8 +702,8 @@ int mbp_gemv_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, floa
   if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
   if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n) return MBP_ERR_SHAPE;
-  return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, w->k / 64, w->k, n_out, x, m, out, ldo, true, geom,
-                stream);
+  return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, w->n_esc, w->k / 64, w->k, n_out, x, m, out, ldo,
+                true, geom, stream);
 }
 
 int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,
@@ -669,11 +713,11 @@ int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int
   if (m < 1) return MBP_ERR_M;
   mbp_gemv_geom g;
   if (!geom) {
-    const int rc = plan_impl(FMT_HILO, w->n / 16, w->k / 64, m, true, &g);
+    const int rc = plan_impl(FMT_HILO, w->n / 16, w->k / 64, m, true, false, &g);
     if (rc) return rc;
     geom = &g;
   }
-  return launch(FMT_HILO, w->units, nullptr, nullptr, nullptr, w->k / 64, w->k, w->n, x, m, out, ldo, true, geom,
+  return launch(FMT_HILO, w->units, nullptr, nullptr, nullptr, 0, w->k / 64, w->k, w->n, x, m, out, ldo, true, geom,
                 stream);
 }
 

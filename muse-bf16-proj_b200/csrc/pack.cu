@@ -237,8 +237,8 @@ __global__ void k_unpack(const uint8_t* __restrict__ units, const uint8_t* __res
   extern __shared__ __align__(16) unsigned char smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long long u = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
-  const uint32_t xr = smem_u32(smem) + warp * kXorWarpBytes;
-  xor_mask_clear(xr, lane);
+  const uint32_t xr = smem_u32(smem) + warp * kMaskUnitBytes;
+  mask_clear(xr, kMaskUnitBytes, lane);
   if (u >= (long long)R * C) return;
   const int r = (int)(u / C), c = (int)(u % C);
   const uint8_t* src = units + (size_t)u * MBP_C12_UNIT_BYTES + lane * 16;
@@ -246,10 +246,14 @@ __global__ void k_unpack(const uint8_t* __restrict__ units, const uint8_t* __res
   const uint4 p1 = *reinterpret_cast<const uint4*>(src + 512);
   const uint4 p2 = *reinterpret_cast<const uint4*>(src + 1024);
   uint32_t A[16];
-  decode_unit(p0, p1, p2, table_lo(bases[r]), table_hi(bases[r]), A);
   EscCursor cur;
   cur.init(esc, esc_off[u], esc_off[u + 1], lane);
-  cur.apply((uint32_t)c, A, xr, lane);
+  uint32_t tgt[1] = {0u};
+  cur.scatter<1>((uint32_t)c, (uint32_t)c + 1, xr, kMaskUnitBytes, lane, tgt);
+  __syncwarp();
+  uint4 m0, m1;
+  take_mask(xr, tgt[0], lane, m0, m1);
+  decode_unit_m(p0, p1, p2, table_lo(bases[r]), table_hi(bases[r]), m0, m1, A);
   const int g = lane >> 2, t = lane & 3;
 #pragma unroll
   for (int rh = 0; rh < 2; ++rh) {
@@ -358,8 +362,8 @@ int mbp_unpack_c12(const mbp_c12* p, uint16_t* w_out, cudaStream_t stream) {
   const int R = p->n / 16, C = p->k / 64;
   const long long NU = (long long)R * C;
   const unsigned blocks = (unsigned)((NU + kWarpsPerCta - 1) / kWarpsPerCta);
-  k_unpack<<<blocks, kWarpsPerCta * 32, kWarpsPerCta * kXorWarpBytes, stream>>>(p->units, p->bases, p->esc_off,
-                                                                                p->esc, R, C, p->k, w_out);
+  k_unpack<<<blocks, kWarpsPerCta * 32, kWarpsPerCta * kMaskUnitBytes, stream>>>(p->units, p->bases, p->esc_off,
+                                                                                 p->esc, R, C, p->k, w_out);
   return cudaGetLastError() == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
 }
 
