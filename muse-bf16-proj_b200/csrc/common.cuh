@@ -117,6 +117,17 @@ MBP_DEV void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// Bulk prefetch of global memory into L2 (a hint: no completion, no ordering).  src 16-byte aligned, bytes % 16 == 0.
+MBP_DEV void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Programmatic dependent launch.  grid_dep_wait returns once every grid this one depends on has completed and
+// its memory is visible (immediately when the launch had no programmatic dependency); grid_dep_launch lets the
+// next grid of the stream be scheduled once every CTA of this grid has called it or exited.
+MBP_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MBP_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 MBP_DEV uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

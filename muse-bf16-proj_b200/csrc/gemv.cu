@@ -21,6 +21,7 @@
 //
 // The same kernel serves the FP32 router (S:854, S:941, S:943, S:5377, S:5424) with hi/lo BF16 units: two
 // mma.sync per k-step into one FP32 accumulator.
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -60,10 +61,23 @@ struct __align__(64) GemvParams {
 // pass's unit loads, B fragments and accumulators fit in 128 registers without spills.
 __host__ __device__ constexpr int kc_for(int fmt, int mt, int rtw) {
   return rtw == 2 ? (fmt == FMT_C12 && mt == 1 ? 2 : 1)
-                  : fmt == FMT_C12 ? (mt == 1 ? 4 : mt == 2 ? 2 : 1) : (mt == 1 ? 2 : 1);
+                  : fmt == FMT_C12 ? (mt <= 2 ? 4 : 1) : (mt == 1 ? 2 : 1);
 }
 __host__ __device__ constexpr int na_for(int fmt, int mt, int rtw) {
   return rtw == 2 ? (mt == 1 ? 2 : 1) : mt == 4 ? 1 : 2 + 2 * (fmt == FMT_C12 && mt == 1);
+}
+// Chunks per escape mask group (a multiple of the pass): the pass itself for one row tile per warp, two chunks
+// (4 unit masks) for two row tiles per warp, whose passes are a single chunk.
+__host__ __device__ constexpr int mg_for(int fmt, int mt, int rtw) {
+  return rtw == 2 && kc_for(fmt, mt, rtw) < 2 ? 2 : kc_for(fmt, mt, rtw);
+}
+
+template <int I, int N, class F>
+MBP_DEV void static_for(F&& f) {
+  if constexpr (I < N) {
+    f(std::integral_constant<int, I>{});
+    static_for<I + 1, N>(f);
+  }
 }
 
 struct Layout {
@@ -71,7 +85,7 @@ struct Layout {
   int xbytes;   // x bytes per stage
   int sbytes;   // stage bytes (multiple of 1024)
   int ring;     // ring bytes (also holds the split-K reduction after the main loop)
-  int mask;     // escape mask bytes per consumer warp: one 1 KB unit mask per unit of a pass (0 without escapes)
+  int mask;     // escape mask bytes per consumer warp: one 1 KB mask per unit of a mask group (0 without escapes)
   int xr_off;   // per-warp escape masks
   int bar_off;  // full[stages], empty[stages]
   int total;    // bytes from the 1024-aligned base
@@ -89,7 +103,7 @@ __host__ __device__ inline Layout make_layout(int fmt, int mt, int rb, int rtw, 
   const int red = (wki + 1) * rb * mt * 32 * 16;
   if (red > ring) ring = red;
   L.ring = (ring + 127) & ~127;
-  L.mask = (fmt == FMT_C12 && esc) ? kc_for(fmt, mt, rtw) * rtw * kMaskUnitBytes : 0;
+  L.mask = (fmt == FMT_C12 && esc) ? mg_for(fmt, mt, rtw) * rtw * kMaskUnitBytes : 0;
   L.xr_off = L.ring;
   L.bar_off = L.xr_off + (rb / rtw) * wki * L.mask;
   L.total = L.bar_off + 2 * stages * 8;
@@ -119,6 +133,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   constexpr int TOK = 8 * MT;
   constexpr int KC = kc_for(FMT, MT, RTW);  // chunks per unrolled pass
   constexpr int NA = na_for(FMT, MT, RTW);  // independent accumulators per (row tile, token tile)
+  constexpr int MG = mg_for(FMT, MT, RTW);  // chunks per escape mask group
+  static_assert(MG % KC == 0, "a mask group is a whole number of passes");
   constexpr int NL = FMT == FMT_C12 ? 3 : 8;         // 16-byte loads per lane per unit
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -137,6 +153,21 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   const int cs = (int)((long long)s * p.C / p.split), ce = (int)((long long)(s + 1) * p.C / p.split);
   const int Lk = (ce - cs + p.wki - 1) / p.wki;  // chunks per K slice
   const int nit = (Lk + p.kci - 1) / p.kci;
+
+  // Launched as a programmatic dependent of the previous kernel in the stream: the packed weights never depend
+  // on it, so the producer warp starts pulling the first stages' weights into L2 while that kernel drains; every
+  // thread then waits for it to complete (x and the output may be its output / input) before any other access.
+  if (warp == nwc) {
+    const int per_it = rvalid * p.wki, npre = min(p.stages, nit) * per_it;
+    for (int i = lane; i < npre; i += 32) {
+      const int it = i / per_it, rr = (i - it * per_it) / p.wki, q = i - it * per_it - rr * p.wki;
+      const int c0 = cs + q * Lk + it * p.kci, e = min(cs + (q + 1) * Lk, ce);
+      const int nk = min(p.kci, e - c0);
+      if (nk > 0) prefetch_l2(p.units + ((size_t)(r0 + rr) * p.C + c0) * UB, (uint32_t)nk * UB);
+    }
+  }
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (tid == 0) {
     for (int i = 0; i < p.stages; ++i) {
@@ -197,7 +228,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
     for (int j = 0; j < RTW; ++j) rvalid_j[j] = wr * RTW + j < rvalid;
     uint32_t T0[RTW], T1[RTW];
     EscCursor cur[RTW];
-    const uint32_t xr = sbase + L.xr_off + warp * L.mask;  // unit mask of (chunk jc, tile j): xr + (jc*RTW + j) KB
+    const uint32_t xr = sbase + L.xr_off + warp * L.mask;  // mask of (group chunk s, tile j): xr + (s*RTW + j) KB
     if constexpr (FMT == FMT_C12) {
       if (L.mask) mask_clear(xr, L.mask, lane);
 #pragma unroll
@@ -224,26 +255,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
     const uint32_t xoff = (uint32_t)(wk * p.kci * L.xplane + g * 128);
     const uint32_t swz0 = ((2 * t) ^ g) << 4, swz1 = ((2 * t + 1) ^ g) << 4;
 
-    // One pass of KC chunks [c0 + cl0, c0 + min(cl0 + KC, nk)).  ESC selects the variant that restores
-    // escapes (one mask scatter and one __syncwarp for the whole pass); a pass whose chunks hold none of this
-    // warp's escapes runs the variant without any escape code.  FULL passes (all KC chunks present, the common
-    // case) are straight-line code, so the compiler interleaves the decode of one unit with the mma of another.
+    // One pass of KC chunks [c0 + cl0, c0 + min(cl0 + KC, nk)), pass PI of its mask group.  ESC selects the
+    // variant that restores escapes from the group's masks; a group whose chunks hold none of this warp's
+    // escapes runs the variant without any escape code.  FULL passes (all KC chunks present, the common case)
+    // are straight-line code, so the compiler interleaves the decode of one unit with the mma of another.
     // A second tile past the block's valid rows (RTW = 2) is decoded from zero tables and never stored.
-    auto pass_fn = [&](const unsigned char* stage, int c0, int cl0, int nk, auto esc_tag, auto full_tag) {
+    auto pass_fn = [&](const unsigned char* stage, int cl0, int nk, const uint32_t(&tgt)[RTW][MG], auto esc_tag,
+                       auto full_tag, auto pi_tag) {
       constexpr bool ESC = decltype(esc_tag)::value;
       constexpr bool FULL = decltype(full_tag)::value;
-      uint32_t tgt[RTW][KC];  // lanes holding escape bytes, per (tile, chunk) of the pass
-      if constexpr (ESC) {
-        const uint32_t cb = (uint32_t)(c0 + cl0), cend = (uint32_t)(c0 + min(cl0 + KC, nk));
-#pragma unroll
-        for (int j = 0; j < RTW; ++j) {
-#pragma unroll
-          for (int jc = 0; jc < KC; ++jc) tgt[j][jc] = 0u;
-          if (cur[j].next_chunk < cend)
-            cur[j].scatter<KC>(cb, cend, xr + (uint32_t)j * kMaskUnitBytes, RTW * kMaskUnitBytes, lane, tgt[j]);
-        }
-        __syncwarp();
-      }
+      constexpr int S0 = decltype(pi_tag)::value * KC;  // first mask slot of this pass
       uint4 u[KC][RTW][NL];  // all units of the pass first: independent shared loads in flight together
 #pragma unroll
       for (int jc = 0; jc < KC; ++jc)
@@ -259,7 +280,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
         for (int jc = 0; jc < KC; ++jc)
 #pragma unroll
           for (int j = 0; j < RTW; ++j)
-            take_mask(xr + (uint32_t)(jc * RTW + j) * kMaskUnitBytes, tgt[j][jc], lane, mk[jc][j][0], mk[jc][j][1]);
+            take_mask(xr + (uint32_t)((S0 + jc) * RTW + j) * kMaskUnitBytes, tgt[j][S0 + jc], lane, mk[jc][j][0],
+                      mk[jc][j][1]);
       }
 #pragma unroll
       for (int jc = 0; jc < KC; ++jc) {
@@ -317,26 +339,44 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
       const unsigned char* stage = smem + st * L.sbytes;
       const int c0 = b + it * p.kci;
       const int nk = rvalid_j[0] ? max(0, min(p.kci, e - c0)) : 0;  // a warp without valid rows only drains
-      for (int cl0 = 0; cl0 < nk; cl0 += KC) {
-        const bool full = cl0 + KC <= nk;
+      // Mask groups of MG chunks: one escape scatter and one __syncwarp per group, then MG / KC passes.
+      for (int g0 = 0; g0 < nk; g0 += MG) {
+        const int gend = min(g0 + MG, nk);
+        uint32_t tgt[RTW][MG];  // lanes holding escape bytes, per (tile, chunk) of the group
         bool esc_here = false;
         if constexpr (FMT == FMT_C12) {
 #pragma unroll
-          for (int j = 0; j < RTW; ++j) esc_here |= (int)cur[j].next_chunk < c0 + min(cl0 + KC, nk);
-        }
-        if constexpr (FMT == FMT_C12) {
+          for (int j = 0; j < RTW; ++j) esc_here |= (int)cur[j].next_chunk < c0 + gend;
           if (esc_here) {
-            if (full)
-              pass_fn(stage, c0, cl0, nk, std::true_type{}, std::true_type{});
-            else
-              pass_fn(stage, c0, cl0, nk, std::true_type{}, std::false_type{});
-            continue;
+#pragma unroll
+            for (int j = 0; j < RTW; ++j) {
+#pragma unroll
+              for (int s = 0; s < MG; ++s) tgt[j][s] = 0u;
+              if ((int)cur[j].next_chunk < c0 + gend)
+                cur[j].scatter<MG>((uint32_t)(c0 + g0), (uint32_t)(c0 + gend), xr + (uint32_t)j * kMaskUnitBytes,
+                                   RTW * kMaskUnitBytes, lane, tgt[j]);
+            }
+            __syncwarp();
           }
         }
-        if (full)
-          pass_fn(stage, c0, cl0, nk, std::false_type{}, std::true_type{});
-        else
-          pass_fn(stage, c0, cl0, nk, std::false_type{}, std::false_type{});
+        static_for<0, MG / KC>([&](auto pi) {
+          const int cl0 = g0 + decltype(pi)::value * KC;
+          if (cl0 >= nk) return;
+          const bool full = cl0 + KC <= nk;
+          if constexpr (FMT == FMT_C12) {
+            if (esc_here) {
+              if (full)
+                pass_fn(stage, cl0, nk, tgt, std::true_type{}, std::true_type{}, pi);
+              else
+                pass_fn(stage, cl0, nk, tgt, std::true_type{}, std::false_type{}, pi);
+              return;
+            }
+          }
+          if (full)
+            pass_fn(stage, cl0, nk, tgt, std::false_type{}, std::true_type{}, pi);
+          else
+            pass_fn(stage, cl0, nk, tgt, std::false_type{}, std::false_type{}, pi);
+        });
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * st);
@@ -542,9 +582,10 @@ int plan_search(int fmt, int Rout, int C, int m, bool f32, bool esc, mbp_gemv_ge
       while (rows_w * wki > kMaxConsumerWarps) --wki;
       if (wki > cpc) wki = cpc;
       const int per_slice = (cpc + wki - 1) / wki;
-      // largest copy whose stage stays <= 96 KB; 3-4 stages when they fit
+      // largest copy whose stage stays <= 96 KB and whose 2-stage ring fits; 3-4 stages when they fit
       int kci = kc;
       while (kci + kc <= 16 && kci < per_slice && rb * wki * (kci + kc) * ub <= 96 * 1024) kci += kc;
+      while (kci > kc && smem_request(make_layout(fmt, mt, rb, rtw, wki, kci, 2, esc)) > kMaxSmem) kci -= kc;
       const int slot_w = rb * wki * kci * ub;
       int st = 2;
       while (st < 4 && (st + 1) * slot_w <= 192 * 1024 &&
@@ -663,8 +704,14 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   cfg.blockDim = dim3(32 * (rows_w * g.wki + 1));
   cfg.dynamicSmemBytes = smem_request(L);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int na = 0;
+  static const bool pdl = getenv("MBP_NO_PDL") == nullptr;  // MBP_NO_PDL set: plain stream serialisation
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   if (g.split > 1) {
     attr[na].id = cudaLaunchAttributeClusterDimension;
     attr[na].val.clusterDim.x = 1;
@@ -686,6 +733,14 @@ int mbp_gemv_plan(int n_out, int k, int m, mbp_gemv_geom* geom) {
   if (n_out <= 0 || n_out % 16 || k <= 0 || k % 64) return MBP_ERR_SHAPE;
   if (m < 1) return MBP_ERR_M;
   return plan_impl(FMT_C12, n_out / 16, k / 64, m, false, true, geom);
+}
+
+int mbp_gemv_plan_ex(int n_out, int k, int m, int flags, mbp_gemv_geom* geom) {
+  if (!geom || (flags & ~(MBP_PLAN_ESCAPES | MBP_PLAN_F32_OUT))) return MBP_ERR_ARG;
+  if (n_out <= 0 || n_out % 16 || k <= 0 || k % 64) return MBP_ERR_SHAPE;
+  if (m < 1) return MBP_ERR_M;
+  return plan_impl(FMT_C12, n_out / 16, k / 64, m, (flags & MBP_PLAN_F32_OUT) != 0, (flags & MBP_PLAN_ESCAPES) != 0,
+                   geom);
 }
 
 int mbp_gemv_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo,

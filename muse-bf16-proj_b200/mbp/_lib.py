@@ -60,6 +60,7 @@ SIGNATURES = [
     ("mbp_unpack_c12", _I, [ctypes.POINTER(C12), _P, _P]),
     ("mbp_pack_hilo", _I, [_P, _I, _I, _P, _P]),
     ("mbp_gemv_plan", _I, [_I, _I, _I, ctypes.POINTER(Geom)]),
+    ("mbp_gemv_plan_ex", _I, [_I, _I, _I, _I, ctypes.POINTER(Geom)]),
     ("mbp_gemv_c12", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, ctypes.POINTER(Geom), _P]),
     ("mbp_gemv_c12_f32", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, ctypes.POINTER(Geom), _P]),
     ("mbp_router_hilo", _I, [ctypes.POINTER(HiLo), _P, _I, _P, _I, ctypes.POINTER(Geom), _P]),

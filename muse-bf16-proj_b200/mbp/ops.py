@@ -112,9 +112,14 @@ def pack_hilo(w: torch.Tensor) -> PackedHiLo:
     return PackedHiLo(units, n, k)
 
 
-def gemv_plan(n_out: int, k: int, m: int) -> Geom:
+PLAN_ESCAPES, PLAN_F32_OUT = 1, 2
+
+
+def gemv_plan(n_out: int, k: int, m: int, escapes: bool = True, f32_out: bool = False) -> Geom:
+    """The launch geometry the GEMV uses for this shape when no geometry is given."""
     g = Geom()
-    check(lib().mbp_gemv_plan(n_out, k, m, ctypes.byref(g)), "mbp_gemv_plan")
+    flags = (PLAN_ESCAPES if escapes else 0) | (PLAN_F32_OUT if f32_out else 0)
+    check(lib().mbp_gemv_plan_ex(n_out, k, m, flags, ctypes.byref(g)), "mbp_gemv_plan_ex")
     return g
 
 
