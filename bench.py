@@ -459,7 +459,7 @@ def run_profile(spec: str, launches: int = 3):
         mbp.kernel_fn({"x": x, "config": {"m": int(m), "n": n, "k": k, "layer": layer}}, st)
     torch.cuda.synchronize()
     assert mbp.device_status() == 0
-    print("profile run ok:", spec, mbp.gemv_plan(n, k, int(m), escapes=st["layers"][layer].n_esc > 0).as_tuple())
+    print("profile run ok:", spec, st["layers"][layer].plan(int(m)).as_tuple())
 
 
 def main():

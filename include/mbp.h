@@ -124,10 +124,11 @@ int mbp_pack_hilo(const float* w, int n, int k, uint8_t* units, cudaStream_t str
  * out BF16 (mbp_gemv_c12) or FP32 (mbp_gemv_c12_f32) row-major with leading dimension ldo (elements).
  * n_out <= n, n_out % 16 == 0 (the reference's unpooler uses the first 1024 rows at M <= 8, S:272-273).
  * m >= 1; m > 32 runs 32-token blocks.  geom may be NULL (planned internally, for the matrix's escape count and
- * the output type).  mbp_gemv_plan plans for a matrix with escapes and BF16 output (valid for every matrix);
- * mbp_gemv_plan_ex takes MBP_PLAN_* flags and returns exactly the geometry a NULL geom would use. */
-#define MBP_PLAN_ESCAPES 1 /* the matrix has escapes (n_esc > 0): consumer warps reserve escape masks */
-#define MBP_PLAN_F32_OUT 2 /* FP32 output (mbp_gemv_c12_f32) */
+ * the output type).  mbp_gemv_plan plans for a matrix with dense escapes and BF16 output (valid for every
+ * matrix); mbp_gemv_plan_ex takes MBP_PLAN_* flags and returns exactly the geometry a NULL geom would use. */
+#define MBP_PLAN_ESCAPES 1       /* the matrix has escapes (n_esc > 0): consumer warps reserve escape masks */
+#define MBP_PLAN_F32_OUT 2       /* FP32 output (mbp_gemv_c12_f32) */
+#define MBP_PLAN_DENSE_ESCAPES 4 /* at least one escape per 1000 weights (n_esc * 1000 >= n * k) */
 int mbp_gemv_plan(int n_out, int k, int m, mbp_gemv_geom* geom);
 int mbp_gemv_plan_ex(int n_out, int k, int m, int flags, mbp_gemv_geom* geom);
 int mbp_gemv_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo,

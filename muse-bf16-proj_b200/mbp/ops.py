@@ -48,6 +48,15 @@ class PackedC12:
         """Bytes a full GEMV streams: units + escape entries (the roofline's algorithmic weight bytes)."""
         return self.units.numel() + self.n_esc * 4
 
+    @property
+    def dense_escapes(self) -> bool:
+        """At least one escape per 1000 weights (the GEMV planner's dense class)."""
+        return self.n_esc * 1000 >= self.n * self.k
+
+    def plan(self, m: int, n_out: int | None = None, f32_out: bool = False) -> Geom:
+        """The geometry `gemv(self, x)` launches with for m tokens."""
+        return gemv_plan(self.n if n_out is None else n_out, self.k, m, self.n_esc > 0, f32_out, self.dense_escapes)
+
 
 @dataclass
 class PackedHiLo:
@@ -112,13 +121,15 @@ def pack_hilo(w: torch.Tensor) -> PackedHiLo:
     return PackedHiLo(units, n, k)
 
 
-PLAN_ESCAPES, PLAN_F32_OUT = 1, 2
+PLAN_ESCAPES, PLAN_F32_OUT, PLAN_DENSE_ESCAPES = 1, 2, 4
 
 
-def gemv_plan(n_out: int, k: int, m: int, escapes: bool = True, f32_out: bool = False) -> Geom:
-    """The launch geometry the GEMV uses for this shape when no geometry is given."""
+def gemv_plan(n_out: int, k: int, m: int, escapes: bool = True, f32_out: bool = False, dense: bool = False) -> Geom:
+    """The launch geometry the GEMV uses for this shape when no geometry is given (`dense`: at least one escape
+    per 1000 weights)."""
     g = Geom()
-    flags = (PLAN_ESCAPES if escapes else 0) | (PLAN_F32_OUT if f32_out else 0)
+    flags = ((PLAN_ESCAPES if escapes or dense else 0) | (PLAN_F32_OUT if f32_out else 0)
+             | (PLAN_DENSE_ESCAPES if dense else 0))
     check(lib().mbp_gemv_plan_ex(n_out, k, m, flags, ctypes.byref(g)), "mbp_gemv_plan_ex")
     return g
 
