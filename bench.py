@@ -459,7 +459,8 @@ def run_profile(spec: str, launches: int = 3):
         mbp.kernel_fn({"x": x, "config": {"m": int(m), "n": n, "k": k, "layer": layer}}, st)
     torch.cuda.synchronize()
     assert mbp.device_status() == 0
-    print("profile run ok:", spec, st["layers"][layer].plan(int(m)).as_tuple())
+    path = st["layers"][layer].plan(int(m)).as_tuple() if int(m) <= mbp.GEMV_MAX_M else "tcgen05 gemm"
+    print("profile run ok:", spec, path)
 
 
 def main():

@@ -57,6 +57,14 @@ MBP_DEV void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// Arrive that cannot issue before `dep` is available.  A consumer handing a TMA-filled stage back passes a value
+// computed from everything it read from the stage: its shared loads have then completed, so the producer's next
+// copy into the stage cannot overwrite data a load has not yet returned (the arrive itself does not wait for
+// outstanding loads).
+MBP_DEV void mbar_arrive_dep(uint32_t bar, uint32_t dep) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar), "r"(dep) : "memory");
+}
+
 MBP_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");

@@ -7,8 +7,9 @@
 //
 // CTA tile: 128 weight rows (8 row tiles) x BN tokens (<= 256) x a K range; `split` CTAs of a cluster share
 // one tile's K range and reduce through distributed shared memory.  Warp roles:
-//   warp 0       TMA producer: per 64-column chunk, one 3-D box of 8 packed units (12 KB) and one 2-D box of
-//                the x tile (BN rows x 128 bytes, 128-byte swizzle), each completing on its ring's mbarrier;
+//   warp 0       TMA producer of the weights: per 64-column chunk, one 3-D box of 8 packed units (12 KB);
+//   warp 18      TMA producer of x: per chunk one 2-D box of the x tile (BN rows x 128 bytes, 128-byte
+//                swizzle); the two rings run independently, so an x stage is refilled as soon as its MMA is done;
 //   warp 1       allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN, K=16, BF16 -> FP32) x4 per chunk,
 //                A = decoded weights and B = x, both K-major SW128 shared-memory descriptors; tcgen05.commit
 //                frees the A and x stages and finally signals the accumulator;
@@ -21,6 +22,7 @@
 #include "escape.cuh"
 #include "tmap.h"
 
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -31,10 +33,11 @@ namespace {
 
 constexpr int kGroups = 2;                 // decoder groups working on alternate chunks
 constexpr int kDecWarps = 8 * kGroups;
-constexpr int kThreads = 32 * (2 + kDecWarps);
+constexpr int kXWarp = 2 + kDecWarps;      // the x producer
+constexpr int kThreads = 32 * (3 + kDecWarps);
 constexpr int kPS = 4;                     // packed ring depth
 constexpr int kAS = 2;                     // decoded-A ring depth
-constexpr int kXS = 3;                     // x ring depth
+constexpr int kXS = 4;                     // x ring depth
 // Decoder group g owns chunks i = g (mod kGroups).  A ring whose barriers the decoders wait on must give every
 // stage to a single group (depth a multiple of kGroups): otherwise a group could wait for use k+1 of a stage
 // while use k, owned by the other group and completed out of order by the TMA engine, is still pending, and
@@ -48,6 +51,7 @@ constexpr int kMaxSmem = 227 * 1024;
 struct __align__(64) GemmParams {
   CUtensorMap wmap;  // units as [R][C][192 x u64], box {192, 1, 8}
   CUtensorMap xmap;  // x [m, k] bf16, box {64 columns, BN rows}, 128-byte swizzle
+  const uint8_t* units;
   const uint8_t* bases;
   const int32_t* esc_off;
   const uint32_t* esc;
@@ -147,6 +151,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   const int nc = ce - cs;
   const uint32_t tmem_cols = p.bn <= 32 ? 32 : p.bn <= 64 ? 64 : p.bn <= 128 ? 128 : 256;
 
+  // Programmatic dependent launch: the packed weights never depend on the previous kernel of the stream, so the
+  // first ring's units are pulled into L2 while it drains; every thread waits for it before touching x or out.
+  if (warp == 0 && lane < 8 * kPS) {
+    const int d = lane & 7, i = lane >> 3;
+    if (rb0 + d < p.Rout && i < nc)
+      prefetch_l2(p.units + ((size_t)(rb0 + d) * C + cs + i) * MBP_C12_UNIT_BYTES, MBP_C12_UNIT_BYTES);
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+
   if (tid == 0) {
     for (int i = 0; i < kPS; ++i) {
       mbar_init(pfull + 8 * i, 1);
@@ -177,19 +191,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- producer ----------------
+    // ---------------- weight producer ----------------
     if (lane == 0) {
       for (int i = 0; i < nc; ++i) {
-        const int ps = i % kPS, xs = i % kXS;
+        const int ps = i % kPS;
         if (i >= kPS && !mbar_wait(pempty + 8 * ps, ((i / kPS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
         mbar_arrive_expect_tx(pfull + 8 * ps, kPackedStage);
         tma_load_3d(base + L.packed + ps * kPackedStage, &p.wmap, 0, cs + i, rb0, pfull + 8 * ps);
+      }
+    }
+    __syncwarp();  // lanes 1-31 wait here for the producing lane
+  } else if (warp == kXWarp) {
+    // ---------------- x producer ----------------
+    if (lane == 0) {
+      for (int i = 0; i < nc; ++i) {
+        const int xs = i % kXS;
         if (i >= kXS && !mbar_wait(xempty + 8 * xs, ((i / kXS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
         mbar_arrive_expect_tx(xfull + 8 * xs, (uint32_t)p.bn * 128);
         tma_load_2d(base + L.x + xs * p.bn * 128, &p.xmap, (cs + i) * 64, tok0, xfull + 8 * xs);
       }
     }
-    __syncwarp();  // lanes 1-31 wait here for the producing lane
+    __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
@@ -243,7 +265,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       const uint4 p0 = *reinterpret_cast<const uint4*>(u);
       const uint4 p1 = *reinterpret_cast<const uint4*>(u + 512);
       const uint4 p2 = *reinterpret_cast<const uint4*>(u + 1024);
-      mbar_arrive(pempty + 8 * ps);
       uint32_t A[16];
       const uint32_t c = (uint32_t)(cs + i);
       if (valid) cur.seek(c, lane);
@@ -257,6 +278,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       } else {
         decode_unit(p0, p1, p2, T0, T1, A);
       }
+      // A[0] depends on p0 and p2, A[8] on p1: all three loads have returned before the stage is handed back
+      mbar_arrive_dep(pempty + 8 * ps, A[0] ^ A[8]);
       if (i >= kAS && !mbar_wait(aempty + 8 * as, ((i / kAS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY)) break;
       unsigned char* a = sm + L.a + as * kAStage;
 #pragma unroll
@@ -271,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
 
   // ---------------- epilogue: TMEM -> registers -> global (or a cluster reduction) ----------------
   // Decoder warps own TMEM lane quadrant (warp % 4); the kDecWarps/4 warps of a quadrant split the columns.
-  const bool epi = warp >= 2;
+  const bool epi = warp >= 2 && warp < 2 + kDecWarps;
   const int q = warp & 3, part = (warp - 2) >> 2, nparts = kDecWarps / 4;
   const int ncol = (p.bn + 31) / 32;
   const int row_l = q * 32 + lane;                 // row inside the 128-row tile
@@ -441,6 +464,7 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   if (!encode_bf16_2d(&p.xmap, x, (uint64_t)m, (uint64_t)w->k, (uint64_t)w->k, (uint32_t)bn, 64u,
                       CU_TENSOR_MAP_SWIZZLE_128B))
     return MBP_ERR_TMAP;
+  p.units = w->units;
   p.bases = w->bases;
   p.esc_off = w->esc_off;
   p.esc = w->esc;
@@ -458,14 +482,20 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int na = 0;
+  static const bool pdl = getenv("MBP_NO_PDL") == nullptr;  // MBP_NO_PDL set: plain stream serialisation
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   if (p.split > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = p.split;
-    na = 1;
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = p.split;
+    ++na;
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;

@@ -378,8 +378,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
             pass_fn(stage, cl0, nk, tgt, std::false_type{}, std::false_type{}, pi);
         });
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8 * st);
+      // Hand the stage back only once every lane's shared loads of it have returned: fold the accumulators (which
+      // depend on all of them) into one word per lane, and let a warp vote gather the lanes before lane 0's arrive.
+      uint32_t dep = 0;
+#pragma unroll
+      for (int j = 0; j < RTW; ++j)
+#pragma unroll
+        for (int a = 0; a < NA; ++a)
+#pragma unroll
+          for (int n = 0; n < MT; ++n)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) dep ^= __float_as_uint(acc[j][a][n][c]);
+      dep = __any_sync(0xffffffffu, dep == 0x7FC00001u);
+      if (lane == 0) mbar_arrive_dep(empty0 + 8 * st, dep);
     }
   }
 
