@@ -40,8 +40,8 @@ METRIC = "µs/call cold-L2 & packed-weight HBM TB/s vs 8 TB/s peak, M=1–256"
 SHAPES = {"qkv_gate": (14336, 6144), "o": (6144, 6144)}
 MS = (1, 8, 16, 32)
 MATS = (("qkv_gate", "plain"), ("o", "plain"), ("qkv_gate", "esc1pct"), ("o", "esc1pct"))
-# DRAM bytes (read + write) of one QKV+gate M=1 launch from ncu (profiles/gemv_qkv_m1.md), per launch
-NCU_TRAFFIC_QKV_M1 = 138322688
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one QKV+gate M=1 launch, from one ncu capture
+NCU_TRAFFIC_QKV_M1 = 136081664
 
 
 def peaks():

@@ -81,11 +81,24 @@ MBP_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase completes or `ns` elapse,
+// instead of spinning through the issue slots of the warps that do the work.
+MBP_DEV bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: returns false (and records `code`) if the phase did not complete within kWaitLimitNs.
 MBP_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
     if (globaltimer() - t0 > kWaitLimitNs) {
       set_status(code);
       return false;
