@@ -150,9 +150,13 @@ def cpu_reference_run(steps: int, warmup: int, sample_rows: int):
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 3))
-    warm = min(args.warmup, 1)
-    v, dt, cores, sample = cpu_reference_run(steps, warm, sample_rows=1024)
+    # exactly --steps timed and --warmup untimed steps; each step is a row sample of the 16 calls (~55 ms for
+    # 1024 rows on 16 cores), shrunk so that the whole run stays near a minute
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    rows = 1024
+    while rows > 16 and (steps + warm) * rows * 55e-3 / 1024 > 60.0:
+        rows //= 2
+    v, dt, cores, sample = cpu_reference_run(steps, warm, sample_rows=rows)
     line = {"metric": METRIC, "value": round(v, 6), "unit": "TB/s", "n_gpus": args.gpus, "steps": steps,
             "warmup": warm, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE.json config 2 recipe)",
