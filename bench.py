@@ -267,24 +267,56 @@ def run_mbp(args, rank, world):
         torch.cuda.empty_cache()
 
     # ---------------- e2e through the public API with host buffers ----------------
+    # Each call: its x travels host -> device on a copy stream, kernel_fn runs on the compute stream as soon as
+    # that copy lands, and its output travels device -> host on a second copy stream, so the 32 copies of a step
+    # overlap the kernels of the other calls (a serving loop's usual double-buffering); the step ends when the
+    # last output is on the host.
+    h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
+
     def api_step():
+        comp = torch.cuda.current_stream()
+        h2d_s.wait_stream(comp)
+        d2h_s.wait_stream(comp)
         for c in calls:
             st = states[(c[1], c[2])]
-            xd = c[7].to(dev, non_blocking=True)
+            with torch.cuda.stream(h2d_s):
+                xd = c[7].to(dev, non_blocking=True)
+            comp.wait_stream(h2d_s)
+            xd.record_stream(comp)
             out = mbp.kernel_fn({"x": xd, "config": {"m": c[3], "n": c[4].n, "k": c[4].k, "layer": c[1]}}, st)
-            c[8].copy_(out, non_blocking=True)
+            d2h_s.wait_stream(comp)
+            with torch.cuda.stream(d2h_s):
+                c[8].copy_(out, non_blocking=True)
+            out.record_stream(d2h_s)
+        comp.wait_stream(h2d_s)
+        comp.wait_stream(d2h_s)
 
     for _ in range(max(1, args.warmup)):
         api_step()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_steps = max(3, min(args.steps, 50))
+    # eager: every call pays Python + launch overhead on the host (reported beside the headline)
     e0.record()
     for _ in range(e2e_steps):
         api_step()
     e1.record()
     torch.cuda.synchronize()
+    eager_ms = e0.elapsed_time(e1) / e2e_steps
+    # headline e2e: the same public-API step (pinned-host -> device copy of x, kernel_fn, device -> pinned-host
+    # copy of the output, per call) captured once in a CUDA graph and replayed, as the reference's harness replays
+    # kernel_fn
+    g_api = graph_of(api_step, side)
+    for _ in range(3):
+        g_api.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        g_api.replay()
+    e1.record()
+    torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    del g_api
     h2d = sum(2 * c[3] * c[4].k for c in calls)
     d2h = sum(2 * c[3] * c[4].n for c in calls)
 
@@ -315,7 +347,10 @@ def run_mbp(args, rank, world):
                          "kernel": "k_gemv, the 8 qkv_gate launches of a step", "peak_kind": f"{peak_kind} hbm_gbs",
                          "frac_of_8tbps": round(achieved / 8000.0, 4)},
             "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                    "timing": "CUDA-graph replay of the public-API step (per call: H2D of x on a copy stream, "
+                              "kernel_fn, D2H of out on a second copy stream, overlapping the other calls)",
+                    "eager_ms_per_step": round(eager_ms, 4)},
             "gpu_launches": len(calls) * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
