@@ -373,7 +373,9 @@ def run_mbp_tp(args, rank, world):
     lins = {}
     for layer, variant in MATS:
         n, k = SHAPES[layer]
-        lins[(layer, variant)] = TPLinear(make_weight(n, k, variant, dev), "column" if layer == "qkv_gate" else "row")
+        lins[(layer, variant)] = TPLinear(make_weight(n, k, variant, dev), "column" if layer == "qkv_gate" else "row",
+                                          transport=args.transport)
+    transport = next(iter(lins.values())).transport
     torch.cuda.empty_cache()
     shard_bytes = {key: torch.tensor([lin.payload_bytes], device=dev) for key, lin in lins.items()}
     for t in shard_bytes.values():
@@ -463,7 +465,9 @@ def run_mbp_tp(args, rank, world):
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: W~N(0,0.02) torch seed 0 (+1% x256 variant, randperm seed 2), x~N(0,1) seed 1",
             "config": {"workload": "config2 decode GEMV step (16 calls), tensor-parallel: qkv_gate column-parallel + "
-                                   "NCCL all-gather, o row-parallel + NCCL all-reduce of FP32 partials",
+                                   "all-gather, o row-parallel + all-reduce of FP32 partials",
+                       "transport": ("GEMV peer stores over NVLink (CUDA IPC) + flag barrier/assemble kernel"
+                                     if transport == "p2p" else "NCCL collectives"),
                        "l2": "cold by construction (>=250 MB of other weights between reuses of a matrix on one GPU "
                              "at N=1; per-GPU shards at N>1)",
                        "timing": ("CUDA-graph replay" if use_graph else "eager launches") +
@@ -475,7 +479,8 @@ def run_mbp_tp(args, rank, world):
             "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
                     "h2d_bytes_per_step": sum(2 * c[4] * c[6] for c in calls),
                     "d2h_bytes_per_step": sum(2 * c[4] * c[5] for c in calls), "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": 2 * len(calls) * args.steps,  # per call: the GEMV + the assemble / BF16-rounding kernel
+            # per call: the GEMV + the finish kernel (p2p) or the assemble / BF16-rounding kernel after NCCL
+            "gpu_launches": 2 * len(calls) * args.steps,
             "clocks": clocks,
             "cpu_baseline": None,
         }
@@ -510,6 +515,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mbp", choices=["mbp", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],
+                    help="N > 1: tensor-parallel exchange (auto = GEMV peer stores on one node)")
     args = ap.parse_args()
     if args.profile:
         run_profile(args.profile)

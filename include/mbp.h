@@ -40,6 +40,7 @@ extern "C" {
 #define MBP_DEV_TIMEOUT_FULL 1   /* consumer gave up waiting for a stage's bytes */
 #define MBP_DEV_TIMEOUT_EMPTY 2  /* producer gave up waiting for a stage to drain */
 #define MBP_DEV_TIMEOUT_MMA 3    /* tensor-core completion did not arrive */
+#define MBP_DEV_TIMEOUT_PEER 4   /* a peer rank's barrier flag did not arrive */
 
 /* ---- weight formats ---- */
 #define MBP_UNIT_ROWS 16
@@ -152,6 +153,49 @@ int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, floa
  * mbp_f32_to_bf16 rounds them to the BF16 output (n % 4 == 0). */
 int mbp_tp_assemble_columns(const uint16_t* gathered, uint16_t* out, int P, int m, int ns, cudaStream_t stream);
 int mbp_f32_to_bf16(const float* in, uint16_t* out, long long n, cudaStream_t stream);
+
+/* Peer-store exchange on one node (NVLink peers mapped through CUDA IPC; plain loads and stores, no multicast).
+ * mbp_ipc_alloc: zeroed device buffer + its 64-byte IPC handle; mbp_ipc_open maps a peer's buffer into this
+ * process (mbp_ipc_close unmaps, mbp_ipc_free releases an own buffer).
+ * mbp_gemv_c12_multi: the GEMV of mbp_gemv_c12(_f32) storing the same result into `nout` (<= 8) outputs with
+ * one leading dimension, outs[0] local, the others peers' buffers; x rows are ldx elements apart (ldx >= k,
+ * ldx % 8 == 0), so a rank reads its column slice of a wider x in place.  out_kind:
+ *   MBP_OUT_BF16 / MBP_OUT_F32  plain [m][ldo] outputs;
+ *   MBP_OUT_TAGGED_BF16X2       64-bit words [m][ldo] (ldo >= n_out/2): word (t, 8*tile + g) = bf16 rows
+ *                               16*tile + g (low half) and 16*tile + g + 8 (high half), tag in the upper 32 bits;
+ *   MBP_OUT_TAGGED_F32          64-bit words [m][ldo] (ldo >= n_out): word (t, row) = f32 bits | tag << 32.
+ * The tagged kinds need `epoch` (the plain kinds ignore it and parity_stride): this call's epoch is
+ * (*epoch + 1), the tag, and every output pointer moves by parity_stride bytes when it is odd (the exchange
+ * buffer mbp_tp_finish with the same counter reads).  A tagged word and its tag travel in one 64-bit store, so
+ * no fence is needed between ranks.
+ * mbp_tp_finish: counter = this rank's MBP_TP_COUNTER_SLOTS epoch slots (zero-initialised device memory, shared
+ * by every exchange of one group); advances the epoch and, by mode:
+ *   MBP_TP_BARRIER      flags[r] = rank r's flag array (8 ints, zero-initialised): announces the epoch to every
+ *                       rank after a system fence that orders this rank's earlier stores (stream order) before
+ *                       it, and waits (bounded, MBP_DEV_TIMEOUT_PEER) until every rank announced it;
+ *   MBP_TP_GATHER_BF16  waits (bounded) until every word of buf's parity half [m][n/2] carries the epoch's tag
+ *                       (written by the P ranks' MBP_OUT_TAGGED_BF16X2 GEMVs) and writes out[m][n] bf16;
+ *   MBP_TP_SUM_F32      waits likewise on P slots [P][m][n] of MBP_OUT_TAGGED_F32 words and writes
+ *                       out[t][i] = bf16(sum_r slot_r[t][i]) in rank order (identical on every rank).
+ * The tagged modes launch as programmatic dependents of the GEMV before them, so they poll while it drains.
+ * Every rank of a group must make the same sequence of calls.  Graph-replayable. */
+#define MBP_TP_COUNTER_SLOTS 64
+#define MBP_TP_BARRIER 0
+#define MBP_TP_GATHER_BF16 1
+#define MBP_TP_SUM_F32 2
+#define MBP_OUT_BF16 0
+#define MBP_OUT_F32 1
+#define MBP_OUT_TAGGED_BF16X2 2
+#define MBP_OUT_TAGGED_F32 3
+int mbp_ipc_alloc(size_t bytes, void** ptr, void* handle64);
+int mbp_ipc_open(const void* handle64, void** ptr);
+int mbp_ipc_close(void* ptr);
+int mbp_ipc_free(void* ptr);
+int mbp_gemv_c12_multi(const mbp_c12* w, const uint16_t* x, int ldx, int m, int n_out, void* const* outs, int nout,
+                       int ldo, int out_kind, const int* epoch, long long parity_stride, const mbp_gemv_geom* geom,
+                       cudaStream_t stream);
+int mbp_tp_finish(int* const* flags, int rank, int P, int* counter, const void* buf, long long parity_stride,
+                  int mode, int m, int n, void* out, cudaStream_t stream);
 
 /* ---- FP32 router through the hi/lo pair (replaces rr_launch / rr_scalar / rr_small S:856-861, routertail
  * S:5424, rwdl S:5377): out_f32[m, n] = x . hi^T + x . lo^T, FP32 accumulation. ---- */

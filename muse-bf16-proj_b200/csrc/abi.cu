@@ -4,6 +4,7 @@
 int mbp_status_pack(int* v, int clear);
 int mbp_status_gemv(int* v, int clear);
 int mbp_status_gemm(int* v, int clear);
+int mbp_status_tp(int* v, int clear);
 
 extern "C" {
 
@@ -24,6 +25,7 @@ int mbp_status(int* status, int clear) {
   int rc = mbp_status_pack(status, clear);
   if (rc == MBP_OK) rc = mbp_status_gemv(status, clear);
   if (rc == MBP_OK) rc = mbp_status_gemm(status, clear);
+  if (rc == MBP_OK) rc = mbp_status_tp(status, clear);
   return rc;
 }
 

@@ -42,6 +42,16 @@ MBP_DEV uint64_t globaltimer() {
 
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s: a wait this long means a lost arrival
 
+// Single-copy-atomic 64-bit accesses at system scope (epoch-tagged words exchanged between GPUs).
+MBP_DEV void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+MBP_DEV uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // ------------------------------------------------------------------------------------------------------------
 // shared memory / mbarrier
 // ------------------------------------------------------------------------------------------------------------

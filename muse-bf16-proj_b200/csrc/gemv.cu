@@ -40,6 +40,7 @@ enum { FMT_C12 = 0, FMT_HILO = 1 };
 constexpr int kMaxThreads = 384;  // 11 consumer warps + 1 producer (up to 168 registers per thread)
 constexpr int kMaxSmem = 227 * 1024;
 constexpr int kMaxConsumerWarps = 11;
+constexpr int kMaxOuts = 8;  // local output + up to 7 peers
 
 struct __align__(64) GemvParams {
   CUtensorMap xmap;  // x [m, k] bf16, box 64 columns x 8*MT rows, 128-byte swizzle
@@ -47,7 +48,14 @@ struct __align__(64) GemvParams {
   const uint8_t* bases;
   const int32_t* esc_off;
   const uint32_t* esc;
-  void* out;
+  void* outs[kMaxOuts];  // outs[0] local; the others peers' buffers (tensor-parallel peer stores), same layout
+  // Tensor-parallel exchange (the tagged output kinds): outputs are epoch-tagged 64-bit words (ldo in words), this
+  // call's epoch is *epoch + 1 and every output pointer moves by parity_stride bytes when it is odd:
+  // MBP_OUT_TAGGED_BF16X2 word (tk, 8*tile + g) = rows 16*tile + g and + 8 as two bf16; MBP_OUT_TAGGED_F32 word
+  // (tk, row) = one f32.  A word and its tag travel in one 64-bit store, so a reader needs no fence.
+  const int* epoch;
+  long long parity_stride;
+  int nout;
   int C;     // 64-column chunks (k / 64)
   int Rout;  // 16-row tiles computed (n_out / 16)
   int m;     // tokens
@@ -125,9 +133,39 @@ struct Fmt<FMT_HILO> {
 
 MBP_DEV void store_out(uint16_t* o, float v) { *o = __bfloat16_as_ushort(__float2bfloat16_rn(v)); }
 MBP_DEV void store_out(float* o, float v) { *o = v; }
+MBP_DEV uint32_t bf16x2_bits(float lo, float hi) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(lo)) | (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16;
+}
 
-template <int FMT, int MT, int RTW, bool F32OUT>
+// The four results (row, tk), (row + 8, tk), (row, tk + 1), (row + 8, tk + 1) of one accumulator as words tagged
+// with `epoch` into every output (the buffer of the epoch's parity).
+template <int OUTK>
+MBP_DEV void emit_tagged(const GemvParams& p, float4 v, int row, int tk, uint32_t epoch) {
+  const uint64_t tag = (uint64_t)epoch << 32;
+  const long long par = (long long)(epoch & 1u) * p.parity_stride;
+  for (int o = 0; o < p.nout; ++o) {
+    uint64_t* out = reinterpret_cast<uint64_t*>(static_cast<char*>(p.outs[o]) + par);
+    if constexpr (OUTK == MBP_OUT_TAGGED_BF16X2) {
+      const int j = (row >> 4) * 8 + (row & 7);  // word of rows (16*tile + g, 16*tile + g + 8), g = row % 8
+      if (tk < p.m) st_relaxed_sys_u64(out + (size_t)tk * p.ldo + j, tag | bf16x2_bits(v.x, v.z));
+      if (tk + 1 < p.m) st_relaxed_sys_u64(out + (size_t)(tk + 1) * p.ldo + j, tag | bf16x2_bits(v.y, v.w));
+    } else {
+      if (tk < p.m) {
+        st_relaxed_sys_u64(out + (size_t)tk * p.ldo + row, tag | __float_as_uint(v.x));
+        st_relaxed_sys_u64(out + (size_t)tk * p.ldo + row + 8, tag | __float_as_uint(v.z));
+      }
+      if (tk + 1 < p.m) {
+        st_relaxed_sys_u64(out + (size_t)(tk + 1) * p.ldo + row, tag | __float_as_uint(v.y));
+        st_relaxed_sys_u64(out + (size_t)(tk + 1) * p.ldo + row + 8, tag | __float_as_uint(v.w));
+      }
+    }
+  }
+}
+
+// OUTK: MBP_OUT_BF16 / MBP_OUT_F32 plain outputs, MBP_OUT_TAGGED_BF16X2 / MBP_OUT_TAGGED_F32 exchange words.
+template <int FMT, int MT, int RTW, int OUTK>
 __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__ GemvParams p) {
+  constexpr bool F32OUT = OUTK == MBP_OUT_F32 || OUTK == MBP_OUT_TAGGED_F32;
   using OutT = typename std::conditional<F32OUT, float, uint16_t>::type;
   constexpr int UB = Fmt<FMT>::UB;
   constexpr int TOK = 8 * MT;
@@ -156,7 +194,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
 
   // Launched as a programmatic dependent of the previous kernel in the stream: the packed weights never depend
   // on it, so the producer warp starts pulling the first stages' weights into L2 while that kernel drains; every
-  // thread then waits for it to complete (x and the output may be its output / input) before any other access.
+  // thread then waits for it to complete (x, the output and the exchange epoch may be its output / input) before
+  // any other access.  (Filling the shared-memory ring itself before the wait measured no faster.)
   if (warp == nwc) {
     const int per_it = rvalid * p.wki, npre = min(p.stages, nit) * per_it;
     for (int i = lane; i < npre; i += 32) {
@@ -416,19 +455,29 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
       }
   }
   __syncthreads();
-  OutT* out = reinterpret_cast<OutT*>(p.out);
+  // The exchange epoch is read after this grid's dependency wait: the exchange's receive kernel, this grid's
+  // dependent, advances the counter only after this grid has completed.
+  uint32_t epoch = 0;
+  if constexpr (OUTK >= MBP_OUT_TAGGED_BF16X2) epoch = (uint32_t)__ldcg(p.epoch) + 1u;
   auto emit = [&](int idx, float4 v) {
     const int ln = idx & 31, rest = idx >> 5, n = rest % MT, rr = rest / MT;
     if (rr >= rvalid) return;
     const int row = (r0 + rr) * 16 + (ln >> 2);
     const int tk = tok0 + n * 8 + 2 * (ln & 3);
-    if (tk < p.m) {
-      store_out(out + (size_t)tk * p.ldo + row, v.x);
-      store_out(out + (size_t)tk * p.ldo + row + 8, v.z);
+    if constexpr (OUTK >= MBP_OUT_TAGGED_BF16X2) {
+      emit_tagged<OUTK>(p, v, row, tk, epoch);
+      return;
     }
-    if (tk + 1 < p.m) {
-      store_out(out + (size_t)(tk + 1) * p.ldo + row, v.y);
-      store_out(out + (size_t)(tk + 1) * p.ldo + row + 8, v.w);
+    for (int o = 0; o < p.nout; ++o) {
+      OutT* out = reinterpret_cast<OutT*>(p.outs[o]);
+      if (tk < p.m) {
+        store_out(out + (size_t)tk * p.ldo + row, v.x);
+        store_out(out + (size_t)tk * p.ldo + row + 8, v.z);
+      }
+      if (tk + 1 < p.m) {
+        store_out(out + (size_t)(tk + 1) * p.ldo + row, v.y);
+        store_out(out + (size_t)(tk + 1) * p.ldo + row + 8, v.w);
+      }
     }
   };
   const int nthr = blockDim.x;
@@ -466,22 +515,33 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
 // ------------------------------------------------------------------------------------------------------------
 using KernelFn = void (*)(GemvParams);
 
-template <int FMT, int MT, int RTW, bool F32>
+template <int FMT, int MT, int RTW, int OUTK>
 KernelFn kernel_ptr() {
-  return reinterpret_cast<KernelFn>(&k_gemv<FMT, MT, RTW, F32>);
+  return reinterpret_cast<KernelFn>(&k_gemv<FMT, MT, RTW, OUTK>);
 }
 
-KernelFn pick(int fmt, int mt, int rtw, bool f32) {
-  if (fmt == FMT_C12) {
-    if (mt == 1 && rtw == 1) return f32 ? kernel_ptr<FMT_C12, 1, 1, true>() : kernel_ptr<FMT_C12, 1, 1, false>();
-    if (mt == 1) return f32 ? kernel_ptr<FMT_C12, 1, 2, true>() : kernel_ptr<FMT_C12, 1, 2, false>();
-    if (mt == 2 && rtw == 1) return f32 ? kernel_ptr<FMT_C12, 2, 1, true>() : kernel_ptr<FMT_C12, 2, 1, false>();
-    if (mt == 2) return f32 ? kernel_ptr<FMT_C12, 2, 2, true>() : kernel_ptr<FMT_C12, 2, 2, false>();
-    return f32 ? kernel_ptr<FMT_C12, 4, 2, true>() : kernel_ptr<FMT_C12, 4, 2, false>();
+template <int MT, int RTW>
+KernelFn pick_c12(int outk) {
+  switch (outk) {
+    case MBP_OUT_F32: return kernel_ptr<FMT_C12, MT, RTW, MBP_OUT_F32>();
+    case MBP_OUT_TAGGED_BF16X2: return kernel_ptr<FMT_C12, MT, RTW, MBP_OUT_TAGGED_BF16X2>();
+    case MBP_OUT_TAGGED_F32: return kernel_ptr<FMT_C12, MT, RTW, MBP_OUT_TAGGED_F32>();
+    default: return kernel_ptr<FMT_C12, MT, RTW, MBP_OUT_BF16>();
   }
-  if (mt == 1) return kernel_ptr<FMT_HILO, 1, 1, true>();
-  if (mt == 2) return kernel_ptr<FMT_HILO, 2, 1, true>();
-  return kernel_ptr<FMT_HILO, 4, 2, true>();
+}
+
+// outk: MBP_OUT_* (the router format always writes plain FP32)
+KernelFn pick(int fmt, int mt, int rtw, int outk) {
+  if (fmt == FMT_C12) {
+    if (mt == 1 && rtw == 1) return pick_c12<1, 1>(outk);
+    if (mt == 1) return pick_c12<1, 2>(outk);
+    if (mt == 2 && rtw == 1) return pick_c12<2, 1>(outk);
+    if (mt == 2) return pick_c12<2, 2>(outk);
+    return pick_c12<4, 2>(outk);
+  }
+  if (mt == 1) return kernel_ptr<FMT_HILO, 1, 1, MBP_OUT_F32>();
+  if (mt == 2) return kernel_ptr<FMT_HILO, 2, 1, MBP_OUT_F32>();
+  return kernel_ptr<FMT_HILO, 4, 2, MBP_OUT_F32>();
 }
 
 int mt_of(int m) { return m <= 8 ? 1 : m <= 16 ? 2 : 4; }
@@ -573,7 +633,7 @@ int plan_search(int fmt, int Rout, int C, int m, bool f32, bool esc, mbp_gemv_ge
   const int ub = ub_of(fmt);
   const int mt = mt_of(m), rtw = rtw_of(mt), tok = 8 * mt, kc = kc_for(fmt, mt, rtw);
   const int zb = (m + tok - 1) / tok;
-  const KernelFn fn = pick(fmt, mt, rtw, f32);
+  const KernelFn fn = pick(fmt, mt, rtw, f32 ? MBP_OUT_F32 : MBP_OUT_BF16);
   const int sms = sm_count();
   const double total = (double)Rout * C * ub * zb;
   double best = 1e30;
@@ -696,12 +756,20 @@ int plan_impl(int fmt, int Rout, int C, int m, bool f32, int esc, mbp_gemv_geom*
 }
 
 int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* esc_off, const uint32_t* esc,
-           int esc_cls, int C, int K, int n_out, const uint16_t* x, int m, void* out, int ldo, bool f32,
-           const mbp_gemv_geom* geom, cudaStream_t stream) {
+           int esc_cls, int C, int K, int n_out, const uint16_t* x, int ldx, int m, void* const* outs, int nout,
+           int ldo, bool f32, const mbp_gemv_geom* geom, cudaStream_t stream, const int* epoch = nullptr,
+           long long parity_stride = 0, int tagged = 0) {
   if (m < 1) return MBP_ERR_M;
+  if (!outs || nout < 1 || nout > kMaxOuts) return MBP_ERR_ARG;
+  if (parity_stride < 0 || (parity_stride & 15)) return MBP_ERR_ALIGN;
+  if (tagged && !epoch) return MBP_ERR_ARG;
+  for (int o = 0; o < nout; ++o) {
+    if (!outs[o]) return MBP_ERR_ARG;
+    if (tagged && ((uintptr_t)outs[o] & 7u)) return MBP_ERR_ALIGN;
+  }
   if (n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
-  if (ldo < n_out) return MBP_ERR_SHAPE;
-  if (((uintptr_t)x & 15u) || ((uintptr_t)units & 15u)) return MBP_ERR_ALIGN;
+  if (ldo < (tagged == MBP_OUT_TAGGED_BF16X2 ? n_out / 2 : n_out)) return MBP_ERR_SHAPE;
+  if (((uintptr_t)x & 15u) || ((uintptr_t)units & 15u) || ldx < K || ldx % 8) return MBP_ERR_ALIGN;
   const int mt = mt_of(m), tok = 8 * mt;
   const int Rout = n_out / 16;
   const bool with_esc = fmt == FMT_C12 && esc_cls != ESC_NONE;
@@ -722,18 +790,21 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   if (nblk > Rout || (Rout + nblk - 1) / nblk > g.rb) return MBP_ERR_SPLIT;  // a block holds at most rb tiles
   const Layout L = make_layout(fmt, mt, g.rb, rtw, g.wki, g.kci, g.stages, with_esc);
   if (smem_request(L) > kMaxSmem) return MBP_ERR_SMEM;
-  const KernelFn fn = pick(fmt, mt, rtw, f32);
+  const KernelFn fn = pick(fmt, mt, rtw, tagged ? tagged : f32 ? MBP_OUT_F32 : MBP_OUT_BF16);
   int rc = ensure_attrs(fn);
   if (rc) return rc;
   GemvParams p;
-  if (!encode_bf16_2d(&p.xmap, x, (uint64_t)m, (uint64_t)K, (uint64_t)K, (uint32_t)tok, 64u,
+  if (!encode_bf16_2d(&p.xmap, x, (uint64_t)m, (uint64_t)K, (uint64_t)ldx, (uint32_t)tok, 64u,
                       CU_TENSOR_MAP_SWIZZLE_128B))
     return MBP_ERR_TMAP;
   p.units = units;
   p.bases = bases;
   p.esc_off = esc_off;
   p.esc = esc;
-  p.out = out;
+  for (int o = 0; o < kMaxOuts; ++o) p.outs[o] = o < nout ? outs[o] : nullptr;
+  p.epoch = epoch;
+  p.parity_stride = epoch ? parity_stride : 0;
+  p.nout = nout;
   p.C = C;
   p.Rout = Rout;
   p.m = m;
@@ -794,8 +865,9 @@ int mbp_gemv_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t
   if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
   if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n) return MBP_ERR_SHAPE;
+  void* outs[1] = {out};
   return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, esc_class(w->n_esc, w->n, w->k), w->k / 64, w->k,
-                n_out, x, m, out, ldo, false, geom, stream);
+                n_out, x, w->k, m, outs, 1, ldo, false, geom, stream);
 }
 
 int mbp_gemv_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
@@ -803,8 +875,22 @@ int mbp_gemv_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, floa
   if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
   if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n) return MBP_ERR_SHAPE;
+  void* outs[1] = {out};
   return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, esc_class(w->n_esc, w->n, w->k), w->k / 64, w->k,
-                n_out, x, m, out, ldo, true, geom, stream);
+                n_out, x, w->k, m, outs, 1, ldo, true, geom, stream);
+}
+
+int mbp_gemv_c12_multi(const mbp_c12* w, const uint16_t* x, int ldx, int m, int n_out, void* const* outs, int nout,
+                       int ldo, int out_kind, const int* epoch, long long parity_stride, const mbp_gemv_geom* geom,
+                       cudaStream_t stream) {
+  if (!w || !w->units || !w->bases || !w->esc_off || !x || !outs) return MBP_ERR_ARG;
+  if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
+  if (out_kind < MBP_OUT_BF16 || out_kind > MBP_OUT_TAGGED_F32) return MBP_ERR_ARG;
+  if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n) return MBP_ERR_SHAPE;
+  const bool f32 = out_kind == MBP_OUT_F32 || out_kind == MBP_OUT_TAGGED_F32;
+  const int tagged = out_kind >= MBP_OUT_TAGGED_BF16X2 ? out_kind : 0;
+  return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, esc_class(w->n_esc, w->n, w->k), w->k / 64, w->k,
+                n_out, x, ldx, m, outs, nout, ldo, f32, geom, stream, epoch, parity_stride, tagged);
 }
 
 int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,
@@ -818,8 +904,9 @@ int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int
     if (rc) return rc;
     geom = &g;
   }
-  return launch(FMT_HILO, w->units, nullptr, nullptr, nullptr, ESC_NONE, w->k / 64, w->k, w->n, x, m, out, ldo, true,
-                geom, stream);
+  void* outs[1] = {out};
+  return launch(FMT_HILO, w->units, nullptr, nullptr, nullptr, ESC_NONE, w->k / 64, w->k, w->n, x, w->k, m, outs, 1,
+                ldo, true, geom, stream);
 }
 
 }  // extern "C"

@@ -4,7 +4,25 @@
 //                            one buffer produces) -> the row-major projection output [m][P*ns]
 //   mbp_f32_to_bf16          round-to-nearest-even conversion of the reduced FP32 partial sums of a
 //                            row-parallel projection to the BF16 output
+//
+// Peer-store exchange (one node, NVLink peers mapped through CUDA IPC; plain loads and stores, no multicast):
+//   mbp_ipc_alloc / mbp_ipc_open / mbp_ipc_close / mbp_ipc_free   exchange buffers and their cross-process
+//                            mappings
+//   mbp_tp_finish            the receive step.  The sending GEMVs (mbp_gemv_c12_multi, tagged outputs) store
+//                            64-bit words that carry the exchange's epoch in their upper half into every rank's
+//                            buffer; the receive kernel polls its own buffer until each word it needs carries
+//                            the epoch, then writes the assembled BF16 columns, or the rank-order sum of the P
+//                            FP32 partials of a row-parallel projection (identical on every rank).  No fence or
+//                            flag round trip: a system-scope fence costs several microseconds on this part, a
+//                            tagged word arrives with its data.  MBP_TP_BARRIER is a plain flag barrier (system
+//                            fence + release / acquire).  The epoch counter lives in device memory, so the
+//                            exchange replays inside a CUDA graph.
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
+
+using namespace mbp;
 
 namespace {
 
@@ -19,13 +37,146 @@ __global__ void k_assemble(const uint4* __restrict__ src, uint4* __restrict__ ds
   }
 }
 
+MBP_DEV uint32_t pack_bf16x2(float a, float b) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(a)) | (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16;
+}
+
 __global__ void k_f32_to_bf16(const float4* __restrict__ src, uint2* __restrict__ dst, long long n4) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
     const float4 v = src[i];
-    const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(v.x)) | (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v.y)) << 16;
-    const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(v.z)) | (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v.w)) << 16;
-    dst[i] = make_uint2(a, b);
+    dst[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
   }
+}
+
+constexpr int kMaxRanks = 8;
+constexpr int kSlots = MBP_TP_COUNTER_SLOTS;  // a receive launch has one block per epoch slot
+constexpr int kRecvThreads = 256;
+
+struct TPFinish {
+  int* flags[kMaxRanks];  // flags[r] = rank r's flag array (kMaxRanks ints), as mapped in this process
+  int* counter;           // this rank's epoch slots (all equal between launches)
+  const uint8_t* buf;     // this rank's exchange buffers: parity 0 at buf, parity 1 at buf + parity_stride
+  long long parity_stride;
+  void* out;
+  int m, n;               // output [m][n]
+  int rank, P, mode;
+};
+
+MBP_DEV int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+MBP_DEV void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Flag barrier (one block; thread i < kSlots advances slot i).  Every rank writes the new epoch into its entry of
+// every rank's flag array -- a system-scope release after a system fence, so this rank's earlier stores (stream
+// order) are visible to a rank that sees the flag -- and waits, bounded, until its own array holds the epoch from
+// every rank.
+__global__ void __launch_bounds__(kSlots) k_tp_barrier(const __grid_constant__ TPFinish s) {
+  const int l = threadIdx.x;
+  const int e = s.counter[l] + 1;
+  s.counter[l] = e;
+  if (l < s.P) {
+    __threadfence_system();
+    st_release_sys(s.flags[l] + s.rank, e);
+    const int* mine = s.flags[s.rank] + l;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(mine) < e) {
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        set_status(MBP_DEV_TIMEOUT_PEER);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+}
+
+// Bounded wait for a tagged word of epoch e (the tag is the upper 32 bits; data and tag arrive in one store).
+MBP_DEV uint64_t wait_tag(const uint64_t* p, uint32_t e, uint64_t& t0, bool& dead) {
+  uint64_t v = ld_relaxed_sys_u64(p);
+  while ((uint32_t)(v >> 32) != e && !dead) {
+    const uint64_t now = globaltimer();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > kWaitLimitNs) {
+      set_status(MBP_DEV_TIMEOUT_PEER);
+      dead = true;
+    }
+    __nanosleep(32);
+    v = ld_relaxed_sys_u64(p);
+  }
+  return v;
+}
+
+// Receive step of a tagged exchange.  Launched as a programmatic dependent of the GEMV that sends this rank's
+// share, so it starts while that GEMV drains; it reads nothing the stream's earlier kernels write except the
+// tagged words, whose tags it checks.  Block b advances epoch slot b when the GEMV has completed; the epoch's
+// parity picks the buffer the GEMVs filled, so back-to-back exchanges and CUDA-graph
+// replays alternate buffers on the device: a rank writes a buffer again only two epochs later, after every rank
+// has finished reading it (its next receive needs this rank's words of the epoch in between, and a GEMV stores
+// its words only after the receive kernel before it has completed).
+__global__ void __launch_bounds__(kRecvThreads) k_tp_recv(const __grid_constant__ TPFinish s) {
+  // No early trigger for the next kernel: launching the next GEMV while this one's sender still streams measured
+  // slower (its CTAs take the SMs the sender's CTAs free and wait there).
+  __shared__ uint32_t epoch;
+  if (threadIdx.x == 0) epoch = (uint32_t)s.counter[blockIdx.x] + 1u;
+  __syncthreads();
+  const uint32_t e = epoch;
+  const uint64_t* words = reinterpret_cast<const uint64_t*>(s.buf + (e & 1u) * s.parity_stride);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long i0 = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  uint64_t t0 = 0;
+  bool dead = false;
+  if (s.mode == MBP_TP_GATHER_BF16) {
+    // item = (token, 16-row tile): 8 words -> 16 bf16
+    const int tiles = s.n / 16;
+    const long long items = (long long)s.m * tiles;
+    for (long long i = i0; i < items; i += stride) {
+      const int t = (int)(i / tiles), tile = (int)(i - (long long)t * tiles);
+      const uint64_t* w = words + (long long)t * (s.n / 2) + tile * 8;
+      uint32_t d[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) d[g] = (uint32_t)wait_tag(w + g, e, t0, dead);
+      uint4 lo, hi;
+      lo.x = (d[0] & 0xffffu) | d[1] << 16;
+      lo.y = (d[2] & 0xffffu) | d[3] << 16;
+      lo.z = (d[4] & 0xffffu) | d[5] << 16;
+      lo.w = (d[6] & 0xffffu) | d[7] << 16;
+      hi.x = (d[0] >> 16) | (d[1] & 0xffff0000u);
+      hi.y = (d[2] >> 16) | (d[3] & 0xffff0000u);
+      hi.z = (d[4] >> 16) | (d[5] & 0xffff0000u);
+      hi.w = (d[6] >> 16) | (d[7] & 0xffff0000u);
+      uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(s.out) + (long long)t * s.n + tile * 16);
+      o[0] = lo;
+      o[1] = hi;
+    }
+  } else {
+    // MBP_TP_SUM_F32: item = (token, 4 columns); P slots of [m][n] words added in rank order
+    const int q4 = s.n / 4;
+    const long long items = (long long)s.m * q4;
+    for (long long i = i0; i < items; i += stride) {
+      const int t = (int)(i / q4), c = (int)(i - (long long)t * q4) * 4;
+      float a[4];
+      for (int r = 0; r < s.P; ++r) {
+        const uint64_t* w = words + ((long long)r * s.m + t) * s.n + c;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float f = __uint_as_float((uint32_t)wait_tag(w + j, e, t0, dead));
+          a[j] = r == 0 ? f : a[j] + f;
+        }
+      }
+      reinterpret_cast<uint2*>(s.out)[i] = make_uint2(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]));
+    }
+  }
+  // Advance this block's epoch slot only once the sending GEMV has completed: it reads slot 0 after its own
+  // dependency wait but lets this grid start without ordering that read first.
+  grid_dep_wait();
+  if (threadIdx.x == 0) s.counter[blockIdx.x] = (int)e;
 }
 
 int blocks_for(long long work) {
@@ -57,4 +208,78 @@ int mbp_f32_to_bf16(const float* in, uint16_t* out, long long n, cudaStream_t st
   return cudaGetLastError() == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
 }
 
+int mbp_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return MBP_ERR_ARG;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return MBP_ERR_LAUNCH;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess ||
+      cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle), p) != cudaSuccess) {
+    cudaFree(p);
+    return MBP_ERR_LAUNCH;
+  }
+  *ptr = p;
+  return MBP_OK;
+}
+
+int mbp_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return MBP_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+}
+
+int mbp_ipc_close(void* ptr) {
+  if (!ptr) return MBP_ERR_ARG;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+}
+
+int mbp_ipc_free(void* ptr) {
+  if (!ptr) return MBP_ERR_ARG;
+  return cudaFree(ptr) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+}
+
+int mbp_tp_finish(int* const* flags, int rank, int P, int* counter, const void* buf, long long parity_stride,
+                  int mode, int m, int n, void* out, cudaStream_t stream) {
+  if (!counter) return MBP_ERR_ARG;
+  if (P < 1 || P > kMaxRanks || rank < 0 || rank >= P) return MBP_ERR_SHAPE;
+  TPFinish s = {};
+  s.counter = counter;
+  s.rank = rank;
+  s.P = P;
+  s.mode = mode;
+  if (mode == MBP_TP_BARRIER) {
+    if (!flags) return MBP_ERR_ARG;
+    for (int r = 0; r < P; ++r) {
+      if (!flags[r]) return MBP_ERR_ARG;
+      s.flags[r] = flags[r];
+    }
+    k_tp_barrier<<<1, kSlots, 0, stream>>>(s);
+    return cudaGetLastError() == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+  }
+  if (mode != MBP_TP_GATHER_BF16 && mode != MBP_TP_SUM_F32) return MBP_ERR_ARG;
+  if (!buf || !out) return MBP_ERR_ARG;
+  if (m < 1 || n < 16 || n % 16 || parity_stride < 0) return MBP_ERR_SHAPE;
+  if (((uintptr_t)buf & 15u) || (parity_stride & 15) || ((uintptr_t)out & 15u)) return MBP_ERR_ALIGN;
+  s.buf = static_cast<const uint8_t*>(buf);
+  s.parity_stride = parity_stride;
+  s.out = out;
+  s.m = m;
+  s.n = n;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kSlots);
+  cfg.blockDim = dim3(kRecvThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  static const bool pdl = getenv("MBP_NO_PDL") == nullptr;  // MBP_NO_PDL set: plain stream serialisation
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, k_tp_recv, s) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+}
+
 }  // extern "C"
+
+int mbp_status_tp(int* v, int clear) { return read_status_here(v, clear); }

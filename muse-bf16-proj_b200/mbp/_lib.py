@@ -20,7 +20,12 @@ STATUS_NAMES = {
 }
 
 DEVICE_STATUS = {1: "consumer timed out waiting for a stage", 2: "producer timed out waiting for a stage to drain",
-                 3: "tensor-core completion timed out"}
+                 3: "tensor-core completion timed out", 4: "a peer rank's barrier flag did not arrive"}
+
+
+TP_COUNTER_SLOTS = 64                                    # MBP_TP_COUNTER_SLOTS
+TP_BARRIER, TP_GATHER_BF16, TP_SUM_F32 = 0, 1, 2         # MBP_TP_* modes of mbp_tp_finish
+OUT_BF16, OUT_F32, OUT_TAGGED_BF16X2, OUT_TAGGED_F32 = 0, 1, 2, 3  # MBP_OUT_* kinds of mbp_gemv_c12_multi
 
 
 class MbpError(RuntimeError):
@@ -66,6 +71,14 @@ SIGNATURES = [
     ("mbp_router_hilo", _I, [ctypes.POINTER(HiLo), _P, _I, _P, _I, ctypes.POINTER(Geom), _P]),
     ("mbp_tp_assemble_columns", _I, [_P, _P, _I, _I, _I, _P]),
     ("mbp_f32_to_bf16", _I, [_P, _P, ctypes.c_longlong, _P]),
+    ("mbp_ipc_alloc", _I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _P]),
+    ("mbp_ipc_open", _I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    ("mbp_ipc_close", _I, [_P]),
+    ("mbp_ipc_free", _I, [_P]),
+    ("mbp_gemv_c12_multi", _I, [ctypes.POINTER(C12), _P, _I, _I, _I, ctypes.POINTER(ctypes.c_void_p), _I, _I, _I,
+                                _P, ctypes.c_longlong, ctypes.POINTER(Geom), _P]),
+    ("mbp_tp_finish", _I, [ctypes.POINTER(ctypes.c_void_p), _I, _I, _P, _P, ctypes.c_longlong, _I, _I, _I, _P,
+                           _P]),
     ("mbp_gemm_c12", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
     ("mbp_gemm_c12_f32", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
 ]

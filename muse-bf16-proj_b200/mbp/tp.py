@@ -14,6 +14,19 @@ The reference is single-GPU; this layer shards its projections across P GPUs of 
 Each rank packs its own shard (per-shard exponent bases and escape lists).  Every rank must issue the same
 collectives in the same order; all of them run on the current CUDA stream, so a step can be captured in a CUDA
 graph.  ``TPPlan`` holds the host-side sharding and assembly rules on their own (tested with gloo CPU ranks).
+
+**Peer-store transport** (``transport="p2p"``, the default on one node, used for the GEMV calls m <= 32): instead
+of a GEMV, an NCCL collective and an assembly kernel, the GEMV stores its result straight into every rank's
+exchange buffer over NVLink (``mbp_gemv_c12_multi``; buffers mapped through CUDA IPC, plain stores, no
+multicast) as 64-bit words whose upper half is the exchange's epoch, and one receive kernel (``mbp_tp_finish``,
+launched as a programmatic dependent so it polls while the GEMV drains) waits until every word it needs carries
+the epoch and writes the output: column-parallel, rank r's GEMV writes its column block of the [m, N] output
+into every rank's buffer and the receive kernel unpacks the assembled buffer; row-parallel, rank r writes its
+FP32 partial into slot r of every rank's [P, m, N] buffer and the receive kernel adds the P slots in rank order
+(the same order, hence the same bits, on every rank) into BF16.  A word and its tag arrive in one store, so no
+system-scope fence (several microseconds each) is needed.  Each layer has two exchange buffers, picked by the
+parity of an epoch counter kept in device memory, so back-to-back calls and CUDA-graph replays never write a
+buffer a peer may still be reading.  The GEMM calls (m > 32) and ``reduce="scatter"`` keep the NCCL path.
 """
 from __future__ import annotations
 
@@ -23,10 +36,92 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-from ._lib import check, lib
+from ._lib import (OUT_TAGGED_BF16X2, OUT_TAGGED_F32, TP_BARRIER, TP_COUNTER_SLOTS, TP_GATHER_BF16, TP_SUM_F32,
+                   check, lib)
 from .ops import BASE_TILE, PackedC12, gemm, gemv, pack_c12
 
 GEMV_MAX_M = 32
+
+
+# ---------------- device memory exchanged between the ranks of a node ----------------
+
+class PeerBuffer:
+    """One zeroed device buffer per rank of `group`, each mapped into every rank (CUDA IPC); ``ptrs[r]`` is rank
+    r's buffer as seen from this process."""
+
+    def __init__(self, nbytes: int, group=None):
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        check(lib().mbp_ipc_alloc(nbytes, ctypes.byref(own), handle), "mbp_ipc_alloc")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.own = own.value
+        self.ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(self.own)
+                continue
+            p = ctypes.c_void_p()
+            check(lib().mbp_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(p)), "mbp_ipc_open")
+            self.ptrs.append(p.value)
+
+    def local_first(self, offset: int = 0):
+        """Pointers (plus a byte offset) with this rank's first, as a ctypes array for mbp_gemv_c12_multi."""
+        order = [self.rank] + [r for r in range(self.world) if r != self.rank]
+        return (ctypes.c_void_p * self.world)(*[self.ptrs[r] + offset for r in order])
+
+
+class _GroupSync:
+    """Exchange state of one process group: every rank's flag array (peer-mapped) and this rank's epoch slots,
+    shared by all peer-store layers of the group (every rank makes the same sequence of exchanges)."""
+
+    def __init__(self, group=None):
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.flags = PeerBuffer(64, group)
+        self.counter = torch.zeros(TP_COUNTER_SLOTS, dtype=torch.int32,
+                                   device=torch.device("cuda", torch.cuda.current_device()))
+        self.flag_ptrs = (ctypes.c_void_p * self.world)(*self.flags.ptrs)
+
+    def finish(self, buf: PeerBuffer | None, parity_stride: int, mode: int, m: int, n: int,
+               out: torch.Tensor | None):
+        check(lib().mbp_tp_finish(self.flag_ptrs, self.rank, self.world, ctypes.c_void_p(self.counter.data_ptr()),
+                                  ctypes.c_void_p(buf.own if buf else 0), parity_stride, mode, m, n,
+                                  ctypes.c_void_p(out.data_ptr() if out is not None else 0), _stream()),
+              "mbp_tp_finish")
+
+    def barrier(self):
+        """Flag barrier of the group on the current stream (orders every rank's earlier stores before it)."""
+        self.finish(None, 0, TP_BARRIER, 0, 0, None)
+
+
+def _same_node(group) -> bool:
+    """True when every rank of `group` drives a different GPU of this host and all pairs are peer-capable (the
+    barrier's spin waits need the ranks on separate GPUs running concurrently)."""
+    import socket
+    world = dist.get_world_size(group)
+    dev = torch.cuda.current_device()
+    me = (socket.gethostname(), str(torch.cuda.get_device_properties(dev).uuid))
+    seen = [None] * world
+    dist.all_gather_object(seen, me, group=group)
+    ok = world <= 8 and len({s[1] for s in seen}) == world and all(s[0] == me[0] for s in seen)
+    if ok:
+        # peers visible to this process by uuid (all of them when ranks share the device list)
+        local = {str(torch.cuda.get_device_properties(i).uuid): i for i in range(torch.cuda.device_count())}
+        ok = all(torch.cuda.can_device_access_peer(dev, local[u]) for _, u in seen if u in local and local[u] != dev)
+    votes = [None] * world
+    dist.all_gather_object(votes, ok, group=group)
+    return all(votes)
+
+
+_SYNCS: dict = {}
+
+
+def _group_sync(group) -> _GroupSync:
+    key = id(group) if group is not None else None
+    if key not in _SYNCS:
+        _SYNCS[key] = _GroupSync(group)
+    return _SYNCS[key]
 
 
 @dataclass(frozen=True)
@@ -82,9 +177,14 @@ def _stream():
 
 
 class TPLinear:
-    """One tensor-parallel projection on this rank's GPU."""
+    """One tensor-parallel projection on this rank's GPU.
 
-    def __init__(self, w: torch.Tensor, mode: str, group=None, reduce: str = "all", base_mode: int = BASE_TILE):
+    ``transport``: "p2p" stores GEMV results straight into the peers' exchange buffers (one node, every pair of
+    GPUs peer-capable), "nccl" runs the GEMV then an NCCL collective, "auto" picks "p2p" when the group spans
+    more than one GPU of this node and NCCL otherwise (the GEMM calls, m > 32, always use NCCL)."""
+
+    def __init__(self, w: torch.Tensor, mode: str, group=None, reduce: str = "all", base_mode: int = BASE_TILE,
+                 transport: str = "auto"):
         self.group = group
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
@@ -92,9 +192,51 @@ class TPLinear:
         self.plan = TPPlan(mode, world, rank, n, k)
         if reduce not in ("all", "scatter"):
             raise ValueError(reduce)
+        if transport not in ("auto", "p2p", "nccl"):
+            raise ValueError(transport)
         self.reduce = reduce
         dev = torch.device("cuda", torch.cuda.current_device())
         self.packed: PackedC12 = pack_c12(self.plan.shard(w.to(dev)), base_mode)
+        if transport == "auto":
+            transport = "p2p" if world > 1 and _same_node(group) else "nccl"
+        self.transport = transport
+        self._xbuf: PeerBuffer | None = None
+        if transport == "p2p" and world > 1:
+            self._setup_p2p(dev)
+
+    def _setup_p2p(self, dev):
+        p = self.plan
+        # exchange buffers of epoch-tagged 64-bit words, two per rank (epoch parity)
+        if p.mode == "column":
+            per = GEMV_MAX_M * (p.n // 2) * 8                                # [m_max][n/2] bf16-pair words
+        else:
+            per = p.world * GEMV_MAX_M * p.n * 8                             # [P][m_max][n] f32 words
+        self._sync = _group_sync(self.group)
+        self._par = -(-per // 256) * 256                                       # parity-1 buffer offset
+        self._xbuf = PeerBuffer(2 * self._par, self.group)
+
+    def _forward_p2p(self, x: torch.Tensor) -> torch.Tensor:
+        p = self.plan
+        m = x.shape[0]
+        buf, sync = self._xbuf, self._sync
+        epoch = ctypes.c_void_p(sync.counter.data_ptr())
+        out = torch.empty((m, p.n), dtype=torch.bfloat16, device=x.device)
+        if p.mode == "column":
+            # this rank's rows [r*ns, (r+1)*ns) are word columns [r*ns/2, (r+1)*ns/2) of every rank's buffer
+            ns = p.n // p.world
+            check(lib().mbp_gemv_c12_multi(ctypes.byref(self.packed.desc), ctypes.c_void_p(x.data_ptr()), p.k, m, ns,
+                                           buf.local_first(p.rank * (ns // 2) * 8), p.world, p.n // 2,
+                                           OUT_TAGGED_BF16X2, epoch, self._par, None, _stream()),
+                  "mbp_gemv_c12_multi")
+            sync.finish(buf, self._par, TP_GATHER_BF16, m, p.n, out)
+            return out
+        # this rank's FP32 partial of all n outputs from its K slice goes to slot r of every rank's buffer
+        ks = p.k // p.world
+        check(lib().mbp_gemv_c12_multi(ctypes.byref(self.packed.desc), ctypes.c_void_p(x.data_ptr() + p.rank * ks * 2),
+                                       p.k, m, p.n, buf.local_first(p.rank * m * p.n * 8), p.world, p.n,
+                                       OUT_TAGGED_F32, epoch, self._par, None, _stream()), "mbp_gemv_c12_multi")
+        sync.finish(buf, self._par, TP_SUM_F32, m, p.n, out)
+        return out
 
     def _local(self, x: torch.Tensor, out_dtype) -> torch.Tensor:
         xs = self.plan.x_slice(x)
@@ -105,6 +247,12 @@ class TPLinear:
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         p = self.plan
         m = x.shape[0]
+        if self._xbuf is not None and 1 <= m <= GEMV_MAX_M and (p.mode == "column" or self.reduce == "all"):
+            if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != p.k or not x.is_contiguous():
+                raise ValueError(f"x must be a contiguous bf16 [m, {p.k}] tensor")
+            if x.device != self.packed.units.device:
+                raise ValueError("x is not on this rank's device")
+            return self._forward_p2p(x)
         if p.mode == "column":
             local = self._local(x, torch.bfloat16)                        # [m, n/P]
             if p.world == 1:
@@ -141,10 +289,12 @@ class TPLinear:
 DEFAULT_MODES = {"qkv_gate": "column", "o": "row", "pooler": "column", "unpooler": "column"}
 
 
-def prepare_tp(weights: dict, group=None, modes: dict | None = None, reduce: str = "all") -> dict:
+def prepare_tp(weights: dict, group=None, modes: dict | None = None, reduce: str = "all",
+               transport: str = "auto") -> dict:
     """``prepare`` for P ranks: every rank passes the full weights; each keeps and packs its shard."""
     modes = dict(DEFAULT_MODES if modes is None else modes)
-    return {"tp": {name: TPLinear(w, modes.get(name, "column"), group, reduce) for name, w in weights.items()}}
+    return {"tp": {name: TPLinear(w, modes.get(name, "column"), group, reduce, transport=transport)
+                   for name, w in weights.items()}}
 
 
 def kernel_fn_tp(data: dict, state: dict) -> torch.Tensor:

@@ -1,4 +1,5 @@
-"""Tensor-parallel projections over NCCL on 2 GPUs (BASELINE config 5 at P=2); skipped with fewer GPUs.
+"""Tensor-parallel projections on 2 GPUs (BASELINE config 5 at P=2), through the NCCL and the peer-store
+transports; skipped with fewer GPUs.
 
 Runs tests/tp_worker.py under torchrun (rendezvous on 127.0.0.1, NVLS off), bounded by a timeout."""
 import os

@@ -1,8 +1,11 @@
-"""Worker of tests/test_gpu_tp.py: one rank of a tensor-parallel check over NCCL (launched by torchrun).
+"""Worker of tests/test_gpu_tp.py: one rank of a tensor-parallel check (launched by torchrun).
 
 column-parallel fused QKV+gate (K=6144, N=14336, all-gather) and row-parallel output
-projection (K=N=6144, all-reduce and reduce-scatter) at M in {1, 32, 256}, checked against the FP32 reference of
-the unsharded projection (rtol 1e-2 / atol 1e-2).  Exits non-zero on any mismatch."""
+projection (K=N=6144, all-reduce and reduce-scatter) at M in {1, 8, 32, 256}, through both transports (NCCL
+collectives, and peer stores from the GEMV plus the flag barrier), checked against the FP32 reference of the
+unsharded projection (rtol 1e-2 / atol 1e-2).  The peer-store path is also checked for: identical bits on every
+rank, identical column outputs to the NCCL path (same per-shard GEMV), back-to-back calls alternating the
+exchange buffers, and replay of a captured CUDA graph.  Exits non-zero on any mismatch."""
 import datetime
 import os
 import sys
@@ -13,6 +16,20 @@ sys.path.insert(0, os.path.join(ROOT, "muse-bf16-proj_b200"))
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
+RTOL = ATOL = 1e-2
+
+
+def _bad(out, ref):
+    err = (out.float() - ref).abs()
+    return int((err > ATOL + RTOL * ref.abs()).sum()) + int((~torch.isfinite(out.float())).sum()), float(err.max())
+
+
+def _same_on_all_ranks(t: torch.Tensor) -> bool:
+    world = dist.get_world_size()
+    got = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(got, t.contiguous())
+    return all(torch.equal(got[0], g) for g in got)
+
 
 def main():
     rank = int(os.environ["RANK"])
@@ -21,35 +38,95 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60))
     import mbp
     from mbp.tp import TPLinear
-    ok = True
+    fails = []
+
+    def fail(msg):
+        fails.append(msg)
+        print(f"rank {rank} {msg}", flush=True)
+
     g = torch.Generator().manual_seed(0)
     w_qkv = (torch.randn(14336, 6144, generator=g) * 0.02).to(torch.bfloat16).cuda()
     w_o = (torch.randn(6144, 6144, generator=g) * 0.02)
     idx = torch.randperm(w_o.numel(), generator=torch.Generator().manual_seed(2))[: w_o.numel() // 100]
     w_o.view(-1)[idx] *= 256
     w_o = w_o.to(torch.bfloat16).cuda()
-    col = TPLinear(w_qkv, "column")
-    row_all = TPLinear(w_o, "row", reduce="all")
-    row_sc = TPLinear(w_o, "row", reduce="scatter")
-    for m in (1, 32, 256):
+    layers = {}
+    for tr in ("nccl", "p2p"):
+        layers[tr] = {"column": TPLinear(w_qkv, "column", transport=tr),
+                      "row-all": TPLinear(w_o, "row", reduce="all", transport=tr)}
+    layers["nccl"]["row-scatter"] = TPLinear(w_o, "row", reduce="scatter", transport="nccl")
+    if layers["p2p"]["column"].transport != "p2p":
+        fail("p2p transport not selected")
+    weights = {"column": w_qkv, "row-all": w_o, "row-scatter": w_o}
+
+    # 1. every layer, every m, against the FP32 reference
+    for m in (1, 8, 32, 256):
         x = torch.randn(m, 6144, generator=torch.Generator().manual_seed(m)).to(torch.bfloat16).cuda()
-        for name, lin, w, cols in (("column", col, w_qkv, None), ("row-all", row_all, w_o, None),
-                                   ("row-scatter", row_sc, w_o, row_sc.plan.scatter_cols())):
-            out = lin(x)
-            ref = x.float() @ w.float().T
-            if cols is not None:
-                ref = ref[:, cols[0]:cols[1]]
-            err = (out.float() - ref).abs()
-            bad = int((err > 1e-2 + 1e-2 * ref.abs()).sum())
-            if bad or not bool(torch.isfinite(out).all()):
-                ok = False
-                print(f"rank {rank} {name} m={m}: {bad} elements outside tolerance, max err {float(err.max())}",
-                      flush=True)
+        for tr, ls in layers.items():
+            for name, lin in ls.items():
+                out = lin(x).clone()
+                ref = x.float() @ weights[name].float().T
+                if name == "row-scatter":
+                    c0, c1 = lin.plan.scatter_cols()
+                    ref = ref[:, c0:c1]
+                bad, mx = _bad(out, ref)
+                if bad:
+                    fail(f"{tr} {name} m={m}: {bad} elements outside tolerance, max err {mx}")
+                if tr == "p2p" and not _same_on_all_ranks(out):
+                    fail(f"p2p {name} m={m}: ranks disagree")
+                if tr == "p2p" and name == "column":
+                    if not torch.equal(out, layers["nccl"]["column"](x)):
+                        fail(f"p2p column m={m}: differs from the NCCL path")
+
+    # 2. back-to-back calls on one stream (the exchange buffers alternate); outputs read before the next call
+    col, row = layers["p2p"]["column"], layers["p2p"]["row-all"]
+    xs = [torch.randn(8, 6144, generator=torch.Generator().manual_seed(100 + i)).to(torch.bfloat16).cuda()
+          for i in range(6)]
+    kept = []
+    for x in xs:
+        a = col(x)
+        kept.append(a.clone())
+        kept.append(row(a[:, :6144].contiguous()).clone())
+    for i, x in enumerate(xs):
+        ref_a = x.float() @ w_qkv.float().T
+        bad, mx = _bad(kept[2 * i], ref_a)
+        if bad:
+            fail(f"p2p back-to-back column call {i}: {bad} bad, max err {mx}")
+        ref_b = kept[2 * i][:, :6144].float() @ w_o.float().T
+        bad, mx = _bad(kept[2 * i + 1], ref_b)
+        if bad:
+            fail(f"p2p back-to-back row call {i}: {bad} bad, max err {mx}")
+
+    # 3. a captured CUDA graph of column -> row, replayed with new inputs
+    xin = torch.zeros(4, 6144, dtype=torch.bfloat16, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            yb = row(col(xin)[:, :6144].contiguous())
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        ya = col(xin)
+        yb = row(ya[:, :6144].contiguous())
+        yc = yb.clone()
+    for i in range(4):
+        xin.copy_(torch.randn(4, 6144, generator=torch.Generator().manual_seed(200 + i)).to(torch.bfloat16))
+        graph.replay()
+        ref_a = xin.float() @ w_qkv.float().T
+        bad, mx = _bad(ya, ref_a)
+        if bad:
+            fail(f"p2p graph replay {i} (column): {bad} bad, max err {mx}")
+        ref_b = ya[:, :6144].float() @ w_o.float().T   # from the projection's own BF16 intermediate
+        bad, mx = _bad(yc, ref_b)
+        if bad:
+            fail(f"p2p graph replay {i} (row): {bad} bad, max err {mx}")
+    del graph
+
     torch.cuda.synchronize()
     if mbp.device_status() != 0:
-        ok = False
-        print(f"rank {rank}: device status set", flush=True)
-    flag = torch.tensor([0 if ok else 1], device="cuda")
+        fail("device status set")
+    flag = torch.tensor([1 if fails else 0], device="cuda")
     dist.all_reduce(flag)
     dist.destroy_process_group()
     if rank == 0:
