@@ -718,6 +718,21 @@ constexpr Tuned kTuned[] = {
     {384, 96, 1, 0, {3, 1, 1, 2, 8, 2, 128}},  {384, 96, 1, 1, {3, 1, 1, 3, 4, 2, 128}},
     {384, 96, 2, 0, {3, 1, 1, 3, 4, 2, 128}},  {384, 96, 2, 1, {3, 1, 1, 3, 4, 2, 128}},
     {384, 96, 4, 0, {12, 2, 4, 1, 4, 2, 32}},  {384, 96, 4, 1, {6, 2, 2, 3, 2, 2, 64}},
+    // tensor-parallel shards of the same projections (column-parallel qkv_gate: n/P rows; row-parallel o: k/P
+    // columns, FP32 partials), P = 2, 4, 8; only where the measured best beat the planner by more than 3%
+    {448, 96, 1, 0, {7, 1, 2, 1, 8, 2, 64}},   {448, 96, 2, 0, {14, 2, 4, 1, 4, 2, 32}},
+    {448, 96, 4, 0, {14, 2, 4, 1, 3, 2, 32}},  {448, 96, 1, 1, {11, 1, 3, 1, 4, 2, 41}},
+    {448, 96, 2, 1, {11, 1, 3, 1, 4, 2, 41}},  {448, 96, 4, 1, {22, 2, 6, 1, 2, 2, 21}},
+    {384, 48, 1, 0, {3, 1, 1, 2, 8, 2, 148}},  {384, 48, 4, 0, {6, 2, 2, 2, 3, 2, 64}},
+    {384, 48, 4, 1, {6, 2, 2, 3, 2, 2, 64}},   {224, 96, 1, 0, {2, 1, 1, 3, 8, 2, 112}},
+    {224, 96, 2, 0, {11, 1, 6, 1, 4, 2, 21}},  {224, 96, 4, 0, {8, 2, 4, 2, 3, 2, 28}},
+    {224, 96, 1, 1, {11, 1, 6, 1, 4, 2, 21}},  {224, 96, 2, 1, {2, 1, 1, 4, 4, 2, 112}},
+    {224, 96, 4, 1, {2, 2, 1, 7, 2, 2, 112}},  {384, 24, 4, 0, {4, 2, 1, 4, 2, 2, 96}},
+    {384, 24, 4, 1, {4, 2, 1, 4, 2, 2, 96}},   {112, 96, 1, 0, {2, 1, 2, 3, 8, 2, 56}},
+    {112, 96, 2, 0, {4, 1, 4, 2, 4, 2, 28}},   {112, 96, 4, 0, {4, 2, 4, 3, 3, 2, 28}},
+    {112, 96, 1, 1, {4, 1, 4, 2, 4, 2, 28}},   {112, 96, 2, 1, {4, 1, 4, 2, 4, 2, 28}},
+    {112, 96, 4, 1, {4, 2, 4, 4, 2, 2, 28}},   {384, 12, 4, 0, {4, 2, 1, 3, 2, 3, 96}},
+    {384, 12, 4, 1, {4, 2, 1, 4, 2, 2, 96}},
 };
 
 std::mutex g_plan_mu;

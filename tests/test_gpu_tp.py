@@ -1,5 +1,5 @@
-"""Tensor-parallel projections on 2 GPUs (BASELINE config 5 at P=2), through the NCCL and the peer-store
-transports; skipped with fewer GPUs.
+"""Tensor-parallel projections on 2, 4 and 8 GPUs, through the NCCL and the peer-store
+transports; each size is skipped with fewer GPUs.
 
 Runs tests/tp_worker.py under torchrun (rendezvous on 127.0.0.1, NVLS off), bounded by a timeout."""
 import os
@@ -23,11 +23,13 @@ def _port():
     return p
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp_two_gpus():
+@pytest.mark.parametrize("nproc", [2, 4, 8])
+def test_tp(nproc):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < nproc:
+        pytest.skip(f"needs {nproc} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "420", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_port()}",
+           f"--nproc-per-node={nproc}", "--master-addr=127.0.0.1", f"--master-port={_port()}",
            os.path.join(ROOT, "tests", "tp_worker.py")]
     res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=480)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
