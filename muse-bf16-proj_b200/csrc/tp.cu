@@ -121,8 +121,6 @@ MBP_DEV uint64_t wait_tag(const uint64_t* p, uint32_t e, uint64_t& t0, bool& dea
 // has finished reading it (its next receive needs this rank's words of the epoch in between, and a GEMV stores
 // its words only after the receive kernel before it has completed).
 __global__ void __launch_bounds__(kRecvThreads) k_tp_recv(const __grid_constant__ TPFinish s) {
-  // No early trigger for the next kernel: launching the next GEMV while this one's sender still streams measured
-  // slower (its CTAs take the SMs the sender's CTAs free and wait there).
   __shared__ uint32_t epoch;
   if (threadIdx.x == 0) epoch = (uint32_t)s.counter[blockIdx.x] + 1u;
   __syncthreads();
@@ -173,6 +171,10 @@ __global__ void __launch_bounds__(kRecvThreads) k_tp_recv(const __grid_constant_
       reinterpret_cast<uint2*>(s.out)[i] = make_uint2(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]));
     }
   }
+  // Every word has arrived: let the next kernel launch (a GEMV prefetches its first weights into L2, then waits
+  // for this grid to complete before it reads its input, this output or the epoch).  Measured at 4 ranks: 400 us
+  // per 16-call step against 405 us when triggered at the start of this kernel and 417 us at its exit.
+  grid_dep_launch();
   // Advance this block's epoch slot only once the sending GEMV has completed: it reads slot 0 after its own
   // dependency wait but lets this grid start without ordering that read first.
   grid_dep_wait();
