@@ -196,7 +196,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   // on it, so the producer warp starts pulling the first stages' weights into L2 while that kernel drains; every
   // thread then waits for it to complete (x, the output and the exchange epoch may be its output / input) before
   // any other access.  (Filling the shared-memory ring itself before the wait measured no faster.)
+  // The ring barriers and the x tensor map do not depend on it either.
+  if (tid == 0) {
+    for (int i = 0; i < p.stages; ++i) {
+      mbar_init(full0 + 8 * i, 1);
+      mbar_init(empty0 + 8 * i, nwc);
+    }
+    fence_mbar_init();
+  }
   if (warp == nwc) {
+    if (lane == 0) prefetch_tmap(&p.xmap);
     const int per_it = rvalid * p.wki, npre = min(p.stages, nit) * per_it;
     for (int i = lane; i < npre; i += 32) {
       const int it = i / per_it, rr = (i - it * per_it) / p.wki, q = i - it * per_it - rr * p.wki;
@@ -205,18 +214,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
       if (nk > 0) prefetch_l2(p.units + ((size_t)(r0 + rr) * p.C + c0) * UB, (uint32_t)nk * UB);
     }
   }
+  __syncthreads();
   grid_dep_wait();
   grid_dep_launch();
-
-  if (tid == 0) {
-    for (int i = 0; i < p.stages; ++i) {
-      mbar_init(full0 + 8 * i, 1);
-      mbar_init(empty0 + 8 * i, nwc);
-    }
-    fence_mbar_init();
-  }
-  if (warp == nwc && lane == 0) prefetch_tmap(&p.xmap);
-  __syncthreads();
 
   float acc[RTW][NA][MT][4];
 #pragma unroll
