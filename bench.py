@@ -490,6 +490,122 @@ def run_mbp_tp(args, rank, world):
     torch.cuda.synchronize()
 
 
+# The reference's published per-shape times (us, NVIDIA H200, v18 submission, results/v18_shapes.csv:2-31) at its
+# own layer shapes: (M, layer) -> us.  Weights: qkv_gate 2304x8192, o 8192x1024, pooler 4096x8192, unpooler
+# 8192x4096 (n = 1024 at M <= 8), router FP32 256x8192.
+REF_SHAPES = {"qkv_gate": (2304, 8192), "o": (8192, 1024), "pooler": (4096, 8192), "unpooler": (8192, 4096),
+              "router": (256, 8192)}
+REF_H200_US = {
+    (1, "qkv_gate"): 9.34, (1, "o"): 5.10, (1, "pooler"): 13.29, (1, "unpooler"): 3.72, (1, "router"): 3.94,
+    (8, "qkv_gate"): 9.69, (8, "o"): 5.50, (8, "pooler"): 13.61, (8, "unpooler"): 4.28, (8, "router"): 4.34,
+    (16, "qkv_gate"): 10.25, (16, "o"): 5.48, (16, "pooler"): 13.98, (16, "unpooler"): 13.74, (16, "router"): 4.23,
+    (32, "qkv_gate"): 12.16, (32, "o"): 5.81, (32, "pooler"): 16.13, (32, "unpooler"): 15.60, (32, "router"): 5.04,
+    (128, "qkv_gate"): 13.99, (128, "o"): 6.89, (128, "pooler"): 20.49, (128, "unpooler"): 19.37,
+    (128, "router"): 6.19,
+    (256, "qkv_gate"): 17.09, (256, "o"): 8.98, (256, "pooler"): 24.19, (256, "unpooler"): 23.32,
+    (256, "router"): 8.44,
+}
+
+
+def run_ref_shapes(reps: int = 200):
+    """--ref-shapes: kernel_fn at the reference's 30 (M, layer) shapes with cold L2, as its judge timed them (CUDA
+    graph of one call with a new output tensor, L2 flushed between calls, fixed replay overhead excluded).  CUDA
+    events on this box resolve 2.048 us, too coarse around a single replay, so each shape is timed by difference:
+    `reps` calls as replays of a graph of 10 x [flush a 256 MB buffer, call] minus the flushes alone, each between
+    one pair of events, divided by `reps`.  One JSON line; the H200 numbers are the reference's, on different
+    hardware (4.8 vs 8 TB/s HBM)."""
+    import torch
+    import mbp
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    ws = {name: (torch.randn(n, k) * 0.02).to(torch.bfloat16).to(dev)
+          for name, (n, k) in REF_SHAPES.items() if name != "router"}
+    ws["router"] = (torch.randn(256, 8192) * 0.01).to(dev)
+    st = mbp.prepare(ws)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    inner = 10  # pairs per graph: a graph replay's duration comes in whole 2.048 us ticks on this box
+
+    def graph_time(fn):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(inner):
+                fn()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps // inner):
+            g.replay()
+        b.record()
+        b.synchronize()
+        del g
+        return a.elapsed_time(b) * 1e3 / (reps // inner * inner)
+
+    # Copies of each layer's packed weights (same descriptors, cloned payload) so that back-to-back calls rotate
+    # over more than 2x L2 of weights: every call reads its weights from HBM, as in a decode loop.
+    from mbp.ops import PackedC12, PackedHiLo
+
+    def copies_of(layer):
+        if layer in st["hilo"]:
+            p = st["hilo"][layer]
+            reps_ = max(2, -(-(256 << 20) // p.units.numel()))
+            ps = [p] + [PackedHiLo(p.units.clone(), p.n, p.k) for _ in range(reps_ - 1)]
+            return [{"layers": {}, "hilo": {layer: q}, "k": st["k"]} for q in ps]
+        p = st["layers"][layer]
+        reps_ = max(2, -(-(256 << 20) // p.units.numel()))
+        ps = [p] + [PackedC12(p.units.clone(), p.bases, p.esc_off, p.esc, p.n, p.k, p.n_esc) for _ in range(reps_ - 1)]
+        return [{"layers": {layer: q}, "hilo": {}, "k": st["k"]} for q in ps]
+
+    rows, ratios = [], []
+    for layer in REF_SHAPES:
+        states = copies_of(layer)
+        for (m, lay), ref_us in REF_H200_US.items():
+            if lay != layer:
+                continue
+            n, k = REF_SHAPES[layer]
+            n_call = 1024 if layer == "unpooler" and m <= 8 else n
+            x = make_x(m, k, dev)
+            data = {"x": x, "config": {"m": m, "n": n_call, "k": k, "layer": layer}}
+
+            def rotate():
+                for s in states:
+                    mbp.kernel_fn(data, s)
+
+            def flush_call():
+                torch.amax(flush)  # read flush: L2 left holding clean lines
+                mbp.kernel_fn(data, st)
+
+            row = {"m": m, "layer": layer, "n": n_call, "k": k,
+                   "us": round(graph_time(rotate) / len(states), 2),
+                   "us_after_flush": round(graph_time(flush_call) - graph_time(lambda: torch.amax(flush)), 2),
+                   "ref_h200_us": ref_us}
+            row["ratio_ref_over_this"] = round(ref_us / row["us"], 3)
+            rows.append(row)
+            ratios.append(ref_us / row["us"])
+        del states
+    assert mbp.device_status() == 0
+    import math
+    geo = math.exp(sum(math.log(r) for r in ratios) / len(ratios))
+    print(json.dumps({"ref_shapes": sorted(rows, key=lambda r: (r["m"], list(REF_SHAPES).index(r["layer"]))),
+                      "geomean_ratio_vs_ref_h200": round(geo, 3),
+                      "method": "us: back-to-back kernel_fn calls in CUDA-graph replays, rotating over copies of the "
+                                "layer's packed weights totalling >= 256 MB (every call reads cold weights), %d "
+                                "calls per copy-cycle group, one event pair; us_after_flush: (10 x [read 256 MB, call]"
+                                " - the reads alone) per call, which adds the kernel-boundary transition after a "
+                                "foreign kernel" % reps}),
+          flush=True)
+
+
 def run_profile(spec: str, launches: int = 3):
     """--profile LAYER:M:VARIANT -- a few launches of one call for an ncu capture (no timing, no output)."""
     import torch
@@ -515,11 +631,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mbp", choices=["mbp", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--ref-shapes", action="store_true",
+                    help="time kernel_fn at the reference's 30 published shapes (one JSON line, not the bench line)")
     ap.add_argument("--transport", default="auto", choices=["auto", "p2p", "nccl"],
                     help="N > 1: tensor-parallel exchange (auto = GEMV peer stores on one node)")
     args = ap.parse_args()
     if args.profile:
         run_profile(args.profile)
+        return
+    if args.ref_shapes:
+        run_ref_shapes()
         return
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

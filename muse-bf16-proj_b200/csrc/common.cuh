@@ -210,6 +210,12 @@ MBP_DEV uint32_t mapa(uint32_t addr, uint32_t rank) {
   return d;
 }
 
+MBP_DEV void st_dsmem_f4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
 MBP_DEV float4 ld_dsmem_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"

@@ -108,7 +108,7 @@ __host__ __device__ inline Layout make_layout(int fmt, int mt, int rb, int rtw, 
   const int wbytes = rb * wki * kci * ub;
   L.sbytes = (L.xbytes + wbytes + 1023) & ~1023;
   int ring = stages * L.sbytes;
-  const int red = (wki + 1) * rb * mt * 32 * 16;
+  const int red = (wki + 1) * rb * mt * 32 * 16 + 256;  // + the split-K slots' rounding (< 16 items)
   if (red > ring) ring = red;
   L.ring = (ring + 127) & ~127;
   L.mask = (fmt == FMT_C12 && esc) ? mg_for(fmt, mt, rtw) * rtw * kMaskUnitBytes : 0;
@@ -435,26 +435,42 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
 
   // ---------------- split-K reduction ----------------
   __syncthreads();  // ring is free: every stage has been consumed
+  // Reduction.  Accumulator (j, n) of consumer warp (wr, wk) is item ((wr*RTW + j)*MT + n)*32 + lane of the CTA
+  // tile (NI items of 4 results).  wki > 1: the K-slice warps add up through shared memory (`red`).  split > 1:
+  // after a cluster barrier (every CTA is past its main loop, so its ring area is free) each CTA pushes its
+  // partial items with distributed-shared-memory stores into the CTA that owns them (1/split of the tile each,
+  // slot = pusher's cluster rank), and after a second barrier every owner adds its slots in rank order from its
+  // own shared memory and stores.  (Pulling the partials with remote loads measured 1-2 us slower per call.)
   const int NI = p.rb * MT * 32;
   float4* red = reinterpret_cast<float4*>(smem);
-  float4* csum = red + (size_t)p.wki * NI;
-  if (warp < nwc) {
+  auto acc_item = [&](int j, int n) {
+    float4 v = make_float4(acc[j][0][n][0], acc[j][0][n][1], acc[j][0][n][2], acc[j][0][n][3]);
 #pragma unroll
-    for (int j = 0; j < RTW; ++j)
+    for (int a = 1; a < NA; ++a) {
+      v.x += acc[j][a][n][0];
+      v.y += acc[j][a][n][1];
+      v.z += acc[j][a][n][2];
+      v.w += acc[j][a][n][3];
+    }
+    return v;
+  };
+  if (p.wki > 1) {
+    if (warp < nwc) {
 #pragma unroll
-      for (int n = 0; n < MT; ++n) {
-        float4 v = make_float4(acc[j][0][n][0], acc[j][0][n][1], acc[j][0][n][2], acc[j][0][n][3]);
+      for (int j = 0; j < RTW; ++j)
 #pragma unroll
-        for (int a = 1; a < NA; ++a) {
-          v.x += acc[j][a][n][0];
-          v.y += acc[j][a][n][1];
-          v.z += acc[j][a][n][2];
-          v.w += acc[j][a][n][3];
-        }
-        red[(size_t)wk * NI + ((wr * RTW + j) * MT + n) * 32 + lane] = v;
-      }
+        for (int n = 0; n < MT; ++n) red[(size_t)wk * NI + ((wr * RTW + j) * MT + n) * 32 + lane] = acc_item(j, n);
+    }
+    __syncthreads();
   }
-  __syncthreads();
+  auto red_item = [&](int idx) {
+    float4 v = red[idx];
+    for (int q = 1; q < p.wki; ++q) {
+      const float4 w = red[(size_t)q * NI + idx];
+      v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+    }
+    return v;
+  };
   // The exchange epoch is read after this grid's dependency wait: the exchange's receive kernel, this grid's
   // dependent, advances the counter only after this grid has completed.
   uint32_t epoch = 0;
@@ -481,32 +497,47 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
     }
   };
   const int nthr = blockDim.x;
-  for (int idx = tid; idx < NI; idx += nthr) {
-    float4 v = red[idx];
-    for (int q = 1; q < p.wki; ++q) {
-      const float4 w = red[(size_t)q * NI + idx];
+  if (p.split == 1) {
+    if (p.wki == 1) {
+      if (warp < nwc) {  // every warp holds complete sums: store straight from registers
+#pragma unroll
+        for (int j = 0; j < RTW; ++j)
+#pragma unroll
+          for (int n = 0; n < MT; ++n) emit(((wr * RTW + j) * MT + n) * 32 + lane, acc_item(j, n));
+      }
+    } else {
+      for (int idx = tid; idx < NI; idx += nthr) emit(idx, red_item(idx));
+    }
+    return;
+  }
+  const uint32_t rank = cluster_rank();
+  const int per = (NI + p.split - 1) / p.split;
+  float4* recv = red + (size_t)(p.wki > 1 ? p.wki : 0) * NI;  // [split][per]: this CTA's slots, after `red`
+  const uint32_t recv_u32 = smem_u32(recv);
+  auto push = [&](int idx, float4 v) {
+    const int o = idx / per;
+    st_dsmem_f4(mapa(recv_u32 + (uint32_t)((int)rank * per + idx - o * per) * 16u, (uint32_t)o), v);
+  };
+  cluster_sync();  // every CTA of the cluster is past its main loop: the slots may be written
+  if (p.wki == 1) {
+    if (warp < nwc) {
+#pragma unroll
+      for (int j = 0; j < RTW; ++j)
+#pragma unroll
+        for (int n = 0; n < MT; ++n) push(((wr * RTW + j) * MT + n) * 32 + lane, acc_item(j, n));
+    }
+  } else {
+    for (int idx = tid; idx < NI; idx += nthr) push(idx, red_item(idx));
+  }
+  cluster_sync();  // every push has landed (release / acquire at cluster scope)
+  const int i0 = (int)rank * per, i1 = min(NI, i0 + per);
+  for (int idx = i0 + tid; idx < i1; idx += nthr) {
+    float4 v = recv[idx - i0];
+    for (int q = 1; q < p.split; ++q) {
+      const float4 w = recv[(size_t)q * per + idx - i0];
       v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
     }
-    if (p.split == 1)
-      emit(idx, v);
-    else
-      csum[idx] = v;
-  }
-  if (p.split > 1) {
-    cluster_sync();
-    const uint32_t rank = cluster_rank();
-    const int per = (NI + p.split - 1) / p.split;
-    const int i0 = (int)rank * per, i1 = min(NI, i0 + per);
-    const uint32_t caddr = smem_u32(csum);
-    for (int idx = i0 + tid; idx < i1; idx += nthr) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int q = 0; q < p.split; ++q) {
-        const float4 w = ld_dsmem_f4(mapa(caddr + (uint32_t)idx * 16, (uint32_t)q));
-        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
-      }
-      emit(idx, v);
-    }
-    cluster_sync();  // keep this CTA's partials alive until every rank has read them
+    emit(idx, v);
   }
 }
 
