@@ -764,6 +764,20 @@ constexpr Tuned kTuned[] = {
     {112, 96, 1, 1, {4, 1, 4, 2, 4, 2, 28}},   {112, 96, 2, 1, {4, 1, 4, 2, 4, 2, 28}},
     {112, 96, 4, 1, {4, 2, 4, 4, 2, 2, 28}},   {384, 12, 4, 0, {4, 2, 1, 3, 2, 3, 96}},
     {384, 12, 4, 1, {4, 2, 1, 4, 2, 2, 96}},
+    // the reference's own layer shapes (qkv_gate 2304x8192, o 8192x1024, pooler 4096x8192, unpooler 8192x4096 and
+    // its first 1024 rows), where the measured best beat the planner by more than 3%
+    {144, 128, 1, 0, {2, 1, 2, 3, 8, 2, 72}},  {144, 128, 2, 0, {2, 1, 2, 2, 8, 2, 72}},
+    {144, 128, 4, 0, {2, 2, 2, 7, 2, 2, 72}},  {512, 16, 1, 0, {4, 1, 1, 1, 8, 2, 128}},
+    {512, 16, 4, 0, {4, 2, 1, 4, 2, 2, 128}},  {256, 128, 1, 0, {2, 1, 1, 3, 8, 2, 148}},
+    {256, 128, 4, 0, {8, 2, 4, 2, 3, 2, 32}},  {512, 64, 4, 0, {4, 2, 1, 3, 3, 2, 128}},
+    {64, 64, 1, 0, {4, 1, 8, 1, 4, 2, 16}},    {64, 64, 2, 0, {4, 1, 8, 1, 4, 2, 16}},
+    {64, 64, 4, 0, {4, 2, 8, 2, 2, 2, 16}},
+};
+// hi/lo router (256 x 8192), M tiles 8 / 16 / 32: 4.95 / 5.23 / 6.56 us against the planner's 9.6 / 10.1 / 7.5 us
+constexpr Tuned kTunedHilo[] = {
+    {16, 128, 1, 0, {1, 1, 8, 2, 4, 2, 16}},
+    {16, 128, 2, 0, {1, 1, 8, 3, 3, 2, 16}},
+    {16, 128, 4, 0, {2, 2, 16, 4, 1, 2, 9}},
 };
 
 std::mutex g_plan_mu;
@@ -784,14 +798,19 @@ int plan_impl(int fmt, int Rout, int C, int m, bool f32, int esc, mbp_gemv_geom*
       return MBP_OK;
     }
   }
-  if (fmt == FMT_C12 && zb == 1) {
-    for (const Tuned& t : kTuned)
+  if (zb == 1) {
+    const bool c12 = fmt == FMT_C12;
+    const Tuned* tab = c12 ? kTuned : kTunedHilo;
+    const size_t nt = c12 ? sizeof(kTuned) / sizeof(Tuned) : sizeof(kTunedHilo) / sizeof(Tuned);
+    for (size_t i = 0; i < nt; ++i) {
+      const Tuned& t = tab[i];
       if (t.Rout == Rout && t.C == C && t.mt == mt && t.dense == (esc == ESC_DENSE)) {
         *g = t.g;
         std::lock_guard<std::mutex> lk(g_plan_mu);
         g_plans[key] = *g;
         return MBP_OK;
       }
+    }
   }
   const int rc = plan_search(fmt, Rout, C, m, f32, esc != ESC_NONE, g);
   if (rc == MBP_OK) {
