@@ -741,6 +741,7 @@ int esc_class(int64_t n_esc, int n, int k) {
 struct Tuned {
   int Rout, C, mt, dense;
   mbp_gemv_geom g;
+  int zb = 1;  // token blocks of 8*mt (grid z): m > 32 launches one wave of CTAs per block
 };
 constexpr Tuned kTuned[] = {
     {896, 96, 1, 0, {7, 1, 1, 1, 8, 2, 128}},  {896, 96, 1, 1, {7, 1, 1, 1, 8, 2, 128}},
@@ -773,11 +774,12 @@ constexpr Tuned kTuned[] = {
     {64, 64, 1, 0, {4, 1, 8, 1, 4, 2, 16}},    {64, 64, 2, 0, {4, 1, 8, 1, 4, 2, 16}},
     {64, 64, 4, 0, {4, 2, 8, 2, 2, 2, 16}},
 };
-// hi/lo router (256 x 8192), M tiles 8 / 16 / 32: 4.95 / 5.23 / 6.56 us against the planner's 9.6 / 10.1 / 7.5 us
+// hi/lo router (256 x 8192), M tiles 8 / 16 / 32: 4.95 / 5.23 / 6.56 us against the planner's 9.6 / 10.1 / 7.5 us;
+// M = 64 / 128 / 256 (2 / 4 / 8 token blocks of 32): 8.05 / 9.62 / 13.77 us against 14.5 / 11.3 / 16.1 us
 constexpr Tuned kTunedHilo[] = {
-    {16, 128, 1, 0, {1, 1, 8, 2, 4, 2, 16}},
-    {16, 128, 2, 0, {1, 1, 8, 3, 3, 2, 16}},
-    {16, 128, 4, 0, {2, 2, 16, 4, 1, 2, 9}},
+    {16, 128, 1, 0, {1, 1, 8, 2, 4, 2, 16}},    {16, 128, 2, 0, {1, 1, 8, 3, 3, 2, 16}},
+    {16, 128, 4, 0, {2, 2, 16, 4, 1, 2, 9}},    {16, 128, 4, 0, {2, 2, 6, 3, 3, 2, 8}, 2},
+    {16, 128, 4, 0, {2, 2, 4, 4, 2, 2, 8}, 4},  {16, 128, 4, 0, {4, 2, 4, 2, 2, 2, 4}, 8},
 };
 
 std::mutex g_plan_mu;
@@ -798,13 +800,13 @@ int plan_impl(int fmt, int Rout, int C, int m, bool f32, int esc, mbp_gemv_geom*
       return MBP_OK;
     }
   }
-  if (zb == 1) {
+  {
     const bool c12 = fmt == FMT_C12;
     const Tuned* tab = c12 ? kTuned : kTunedHilo;
     const size_t nt = c12 ? sizeof(kTuned) / sizeof(Tuned) : sizeof(kTunedHilo) / sizeof(Tuned);
     for (size_t i = 0; i < nt; ++i) {
       const Tuned& t = tab[i];
-      if (t.Rout == Rout && t.C == C && t.mt == mt && t.dense == (esc == ESC_DENSE)) {
+      if (t.Rout == Rout && t.C == C && t.mt == mt && t.zb == zb && t.dense == (esc == ESC_DENSE)) {
         *g = t.g;
         std::lock_guard<std::mutex> lk(g_plan_mu);
         g_plans[key] = *g;
