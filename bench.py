@@ -522,7 +522,24 @@ def run_ref_shapes(reps: int = 200):
     ws = {name: (torch.randn(n, k) * 0.02).to(torch.bfloat16).to(dev)
           for name, (n, k) in REF_SHAPES.items() if name != "router"}
     ws["router"] = (torch.randn(256, 8192) * 0.01).to(dev)
-    st = mbp.prepare(ws)
+    mbp.prepare({"o": ws["o"]})  # library load and first-call setup, outside the prepare timings
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    st = mbp.prepare(ws)  # GPU packing + device round-trip verification of all five layers
+    torch.cuda.synchronize()
+    prep = {"prepare_s": round(time.perf_counter() - t0, 3)}
+    with tempfile.TemporaryDirectory() as td:
+        cache = os.path.join(td, "weights.mbp")
+        t0 = time.perf_counter()
+        mbp.prepare(ws, cache=cache)
+        torch.cuda.synchronize()
+        prep["prepare_and_write_cache_s"] = round(time.perf_counter() - t0, 3)
+        t0 = time.perf_counter()
+        mbp.prepare(ws, cache=cache)
+        torch.cuda.synchronize()
+        prep["prepare_from_cache_s"] = round(time.perf_counter() - t0, 3)
+        prep["cache_bytes"] = os.path.getsize(cache)
+    prep["reference_h200_prepare_s"] = 53.80  # cold prepare of the reference, results/v18.json:15
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     inner = 10  # pairs per graph: a graph replay's duration comes in whole 2.048 us ticks on this box
@@ -597,7 +614,7 @@ def run_ref_shapes(reps: int = 200):
     import math
     geo = math.exp(sum(math.log(r) for r in ratios) / len(ratios))
     print(json.dumps({"ref_shapes": sorted(rows, key=lambda r: (r["m"], list(REF_SHAPES).index(r["layer"]))),
-                      "geomean_ratio_vs_ref_h200": round(geo, 3),
+                      "geomean_ratio_vs_ref_h200": round(geo, 3), "prepare": prep,
                       "method": "us: back-to-back kernel_fn calls in CUDA-graph replays, rotating over copies of the "
                                 "layer's packed weights totalling >= 256 MB (every call reads cold weights), %d "
                                 "calls per copy-cycle group, one event pair; us_after_flush: (10 x [read 256 MB, call]"

@@ -18,12 +18,15 @@ from typing import TypedDict
 
 import torch
 
+from . import store
 from ._lib import MbpError, device_status, lib
 from .ops import (BASE_MATRIX, BASE_TILE, PackedC12, PackedHiLo, gemm, gemv, gemv_plan, pack_c12, pack_hilo,
                   router, unpack_c12)
+from .store import load_packed, save_packed
 
 __all__ = ["Weights", "Config", "Inputs", "prepare", "kernel_fn", "MbpError", "PackedC12", "PackedHiLo", "pack_c12",
-           "unpack_c12", "pack_hilo", "gemv", "gemm", "gemv_plan", "router", "device_status", "BASE_MATRIX", "BASE_TILE"]
+           "unpack_c12", "pack_hilo", "gemv", "gemm", "gemv_plan", "router", "device_status", "BASE_MATRIX", "BASE_TILE",
+           "save_packed", "load_packed", "store"]
 
 LAYERS = ("qkv_gate", "o", "pooler", "unpooler", "router")
 GEMV_MAX_M = 32  # the reference's decode/verify boundary: small-M GEMVs up to 32 tokens (SM_MAX_M, S:252)
@@ -49,9 +52,18 @@ class Inputs(TypedDict):
     config: Config
 
 
-def prepare(weights: Weights, base_mode: int = BASE_TILE, verify: bool = True) -> dict:
+def prepare(weights: Weights, base_mode: int = BASE_TILE, verify: bool = True, cache: str | None = None) -> dict:
     """Packs every layer on its device.  ``weights`` may hold any subset of the five layers and any shapes with
-    rows % 16 == 0 and columns % 64 == 0.  BF16 tensors take the 12-bit path, FP32 tensors the hi/lo path."""
+    rows % 16 == 0 and columns % 64 == 0.  BF16 tensors take the 12-bit path, FP32 tensors the hi/lo path.
+
+    ``cache``: path of a packed weight file (``mbp.store``).  When it holds exactly these layers (same
+    fingerprints and base mode) the state is loaded from it instead of packing; otherwise the layers are packed
+    (and verified) and the file is written."""
+    fps = None
+    if cache is not None:
+        fps = {name: store.fingerprint(w) for name, w in weights.items()}
+        if store.matches(cache, fps, base_mode):
+            return store.load_packed(cache, {name: w.device for name, w in weights.items()})
     state: dict = {"layers": {}, "hilo": {}, "k": {}}
     for name, w in weights.items():
         if not isinstance(w, torch.Tensor) or not w.is_cuda:
@@ -70,6 +82,8 @@ def prepare(weights: Weights, base_mode: int = BASE_TILE, verify: bool = True) -
             else:
                 raise ValueError(f"layer {name}: unsupported dtype {w.dtype}")
             state["k"][name] = w.shape[1]
+    if cache is not None:
+        store.save_packed(state, cache, fps, base_mode)
     return state
 
 

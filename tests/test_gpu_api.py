@@ -61,3 +61,33 @@ def test_reference_spike_recipe(state_and_weights):
         d = (out.double() - ref)
         assert float(d[m - 1].norm() / ref[m - 1].norm()) <= 2.5e-4
         assert_reference_norms(out, ref)
+
+
+def test_prepare_cache_round_trip(tmp_path, monkeypatch):
+    """prepare(weights, cache=path): packs and writes on the first call, loads the same bytes on the next (no
+    packing), and re-packs when a weight changes."""
+    import mbp
+    from mbp import ops
+    ws = {"o": weight(1024, 512, seed=3, escape_frac=0.01), "router": (torch.randn(256, 512) * 0.01).cuda()}
+    path = str(tmp_path / "w.mbp")
+    st1 = mbp.prepare(ws, cache=path)
+    packs = []
+    real_c12, real_hilo = ops.pack_c12, ops.pack_hilo
+    monkeypatch.setattr(mbp, "pack_c12", lambda *a, **k: packs.append(1) or real_c12(*a, **k))
+    monkeypatch.setattr(mbp, "pack_hilo", lambda *a, **k: packs.append(1) or real_hilo(*a, **k))
+    st2 = mbp.prepare(ws, cache=path)
+    assert packs == []
+    for name in ("units", "bases", "esc_off", "esc"):
+        assert torch.equal(getattr(st1["layers"]["o"], name), getattr(st2["layers"]["o"], name))
+    assert torch.equal(st1["hilo"]["router"].units, st2["hilo"]["router"].units)
+    x = tokens(8, 512, seed=4)
+    for layer, n in (("o", 1024), ("router", 256)):
+        data = {"x": x, "config": {"m": 8, "n": n, "k": 512, "layer": layer}}
+        assert torch.equal(mbp.kernel_fn(data, st1), mbp.kernel_fn(data, st2))
+    ws2 = dict(ws, o=ws["o"].clone())
+    ws2["o"][5, 7] = -ws2["o"][5, 7] + 1
+    st3 = mbp.prepare(ws2, cache=path)
+    assert len(packs) == 2  # every layer is packed again and the file rewritten
+    data = {"x": x, "config": {"m": 8, "n": 1024, "k": 512, "layer": "o"}}
+    assert_close_bf16(mbp.kernel_fn(data, st3), x.float() @ ws2["o"].float().T)
+    assert mbp.device_status() == 0
