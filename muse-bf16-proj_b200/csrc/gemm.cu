@@ -336,8 +336,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         if (row < p.Rout * 16) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
+            // columns past the tile's bn tokens (bn % 32 != 0) belong to the next token tile's CTA
             const int tok = tok0 + cc * 32 + j;
-            if (tok < p.m) store_elem(p, tok, row, __uint_as_float(v[j]));
+            if (cc * 32 + j < p.bn && tok < p.m) store_elem(p, tok, row, __uint_as_float(v[j]));
           }
         }
       }
@@ -370,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         s += f;
       }
       const int tok = tok0 + c, grow = rb0 * 16 + r;
-      if (tok < p.m && grow < p.Rout * 16) store_elem(p, tok, grow, s);
+      if (c < p.bn && tok < p.m && grow < p.Rout * 16) store_elem(p, tok, grow, s);
     }
     cluster_sync();  // keep this CTA's partials alive until every rank has read them
   }
@@ -473,7 +474,23 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   if (m < 1) return MBP_ERR_M;
   if (ldo < n_out) return MBP_ERR_SHAPE;
   if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u)) return MBP_ERR_ALIGN;
-  const int bn = m >= 256 ? 256 : ((m + 15) / 16) * 16;
+  // Token tile: all tokens up to 256.  Short K (<= 2048): a cluster split-K's reduction costs more than its
+  // short main loop saves, so smaller token tiles fill the SMs instead, down to 64 while one wave holds them
+  // (measured at M=256: o 8192x1024 11.5 us with 128-token tiles against 16.9 us with a 2-way K split).
+  int bn = m >= 256 ? 256 : ((m + 15) / 16) * 16;
+  if (w->k / 64 <= 32) {
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int row_blocks = (n_out / 16 + 7) / 8;
+    int ntok = (m + bn - 1) / bn;
+    for (;;) {  // double the token tiles (balanced, multiples of 16 tokens) while they stay >= 64 and one wave
+      const int t2 = 2 * ntok, bn2 = ((m + t2 - 1) / t2 + 15) / 16 * 16;
+      if (bn2 < 64 || row_blocks * ((m + bn2 - 1) / bn2) > sms) break;
+      ntok = t2;
+      bn = bn2;
+    }
+  }
   const GLayout L = gemm_layout(bn);
   const int smem = L.total + 1024;
   if (smem > kMaxSmem) return MBP_ERR_SMEM;
