@@ -18,8 +18,10 @@ roofline   = the QKV+gate GEMV launches against the measured HBM copy bandwidth 
 --impl reference: the reference path's CPU implementation -- this build's C port of the oracle (decode +
 FP32 accumulate), all host threads -- on a bounded row sample of the same 16 calls, rank 0 only.
 Multi-GPU (torchrun, N > 1): the same step with every projection tensor-parallel over the N ranks (QKV+gate
-column-parallel + NCCL all-gather, O row-parallel + NCCL all-reduce): total work fixed ("strong" scaling),
-device time = max over ranks.
+column-parallel + all-gather, O row-parallel + all-reduce, exchanged by the GEMV's peer stores over NVLink;
+`--transport nccl` for NCCL collectives): total work fixed ("strong" scaling), device time = max over ranks.
+--ref-shapes: kernel_fn at the reference's 30 published (M, layer) shapes against its H200 numbers (one JSON
+line, not the bench line).
 """
 from __future__ import annotations
 
@@ -361,8 +363,9 @@ def run_mbp(args, rank, world):
 
 def run_mbp_tp(args, rank, world):
     """N > 1: the same 16-call step, each projection tensor-parallel over the N ranks (BASELINE config 5 layout:
-    QKV+gate column-parallel + NCCL all-gather, O row-parallel + NCCL all-reduce of FP32 partials).  Total work is
-    fixed (strong scaling); value = packed bytes of the unsharded layers per step / step time (max over ranks)."""
+    QKV+gate column-parallel + all-gather, O row-parallel + all-reduce of FP32 partials; by default through the
+    GEMV's peer stores and the receive kernel, `--transport nccl` for NCCL collectives).  Total work is fixed
+    (strong scaling); value = packed bytes of the unsharded layers per step / step time (max over ranks)."""
     import torch
     import torch.distributed as dist
     import mbp
@@ -434,28 +437,58 @@ def run_mbp_tp(args, rank, world):
     step_ms = float(t.item())
     assert mbp.device_status() == 0
 
-    # e2e: host x in, host output back, every call, eager
+    # e2e: host x in, host output back, every call, through the layers' public forward: as at N = 1, each call's
+    # x travels host -> device on a copy stream and its output device -> host on a second one, overlapping the
+    # other calls, and the step is captured once in a CUDA graph and replayed (the eager time is reported beside)
     hx = [c[2].cpu().pin_memory() for c in calls]
     ho = [torch.empty((c[4], c[5]), dtype=torch.bfloat16).pin_memory() for c in calls]
+    h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
 
     def api_step():
+        comp = torch.cuda.current_stream()
+        h2d_s.wait_stream(comp)
+        d2h_s.wait_stream(comp)
         for c, xh, oh in zip(calls, hx, ho):
-            out = c[1](xh.to(dev, non_blocking=True))
-            oh.copy_(out, non_blocking=True)
+            with torch.cuda.stream(h2d_s):
+                xd = xh.to(dev, non_blocking=True)
+            comp.wait_stream(h2d_s)
+            xd.record_stream(comp)
+            out = c[1](xd)
+            d2h_s.wait_stream(comp)
+            with torch.cuda.stream(d2h_s):
+                oh.copy_(out, non_blocking=True)
+            out.record_stream(d2h_s)
+        comp.wait_stream(h2d_s)
+        comp.wait_stream(d2h_s)
+
+    def timed_max(run, n):
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / n], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     api_step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_steps = max(3, min(args.steps, 20))
-    e0.record()
-    for _ in range(e2e_steps):
-        api_step()
-    e1.record()
-    torch.cuda.synchronize()
-    te = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
-    dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item())
+    eager_e2e_ms = timed_max(api_step, e2e_steps)
+    g_api = None
+    if use_graph:
+        side2 = torch.cuda.Stream()
+        side2.wait_stream(torch.cuda.current_stream())
+        g_api = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side2):
+            with torch.cuda.graph(g_api, stream=side2):
+                api_step()
+        torch.cuda.synchronize()
+        for _ in range(3):
+            g_api.replay()
+    e2e_ms = timed_max(g_api.replay, e2e_steps) if g_api is not None else eager_e2e_ms
     hbm, peak_kind = peaks()
     if rank == 0:
         value = step_bytes / (step_ms * 1e-3) / 1e12
@@ -478,7 +511,11 @@ def run_mbp_tp(args, rank, world):
                          "kernel": "whole step per GPU (GEMV + collectives)", "peak_kind": f"{peak_kind} hbm_gbs"},
             "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
                     "h2d_bytes_per_step": sum(2 * c[4] * c[6] for c in calls),
-                    "d2h_bytes_per_step": sum(2 * c[4] * c[5] for c in calls), "ms_per_step": round(e2e_ms, 4)},
+                    "d2h_bytes_per_step": sum(2 * c[4] * c[5] for c in calls), "ms_per_step": round(e2e_ms, 4),
+                    "timing": ("CUDA-graph replay" if g_api is not None else "eager launches") +
+                              " of the public-API step (per call: H2D of x on a copy stream, the layer's forward, "
+                              "D2H of out on a second copy stream, overlapping the other calls), max over ranks",
+                    "eager_ms_per_step": round(eager_e2e_ms, 4)},
             # per call: the GEMV + the finish kernel (p2p) or the assemble / BF16-rounding kernel after NCCL
             "gpu_launches": 2 * len(calls) * args.steps,
             "clocks": clocks,
@@ -487,6 +524,8 @@ def run_mbp_tp(args, rank, world):
         print(json.dumps(line), flush=True)
     if g is not None:
         del g
+    if g_api is not None:
+        del g_api
     torch.cuda.synchronize()
 
 
