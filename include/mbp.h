@@ -197,6 +197,26 @@ int mbp_gemv_c12_multi(const mbp_c12* w, const uint16_t* x, int ldx, int m, int 
 int mbp_tp_finish(int* const* flags, int rank, int P, int* counter, const void* buf, long long parity_stride,
                   int mode, int m, int n, void* out, cudaStream_t stream);
 
+/* Tensor-parallel projection in ONE kernel per call: the GEMV of this rank's shard stores its results as
+ * epoch-tagged words into every rank's exchange buffer (plain NVLink stores), then each CTA waits (bounded,
+ * MBP_DEV_TIMEOUT_PEER) for the same tiles from the other ranks in its own buffer and writes them into `out`
+ * [m][n] (BF16): gathered columns (MBP_TP_GATHER_BF16, column-parallel: w holds rows [rank*n/P, (rank+1)*n/P))
+ * or the rank-order sum of the FP32 partials (MBP_TP_SUM_F32, row-parallel: w holds n rows and x's columns
+ * [rank*k, (rank+1)*k) for w's k, read in place through ldx).  The grid's last CTA advances the epoch (counter:
+ * MBP_TP_COUNTER_SLOTS slots + one ticket int, zero-initialised).  Exchange buffers: two parity halves of
+ * m*n/2 (gather) or P*m*n (sum) 64-bit words each.  Every rank makes the same sequence of calls; each rank's
+ * grid must fit one wave (the planner's geometries do); graph-replayable. */
+typedef struct {
+  void* bufs[8];            /* rank r's exchange buffer as mapped in this process, r < P */
+  long long parity_stride;  /* bytes between a buffer's two parity halves (multiple of 16) */
+  int* counter;             /* this rank's epoch slots and ticket */
+  int rank, P;
+  int mode;                 /* MBP_TP_GATHER_BF16 or MBP_TP_SUM_F32 */
+  int n;                    /* output columns of the whole projection */
+} mbp_tp_exchange;
+int mbp_gemv_c12_tp(const mbp_c12* w, const uint16_t* x, int ldx, int m, const mbp_tp_exchange* ex, uint16_t* out,
+                    const mbp_gemv_geom* geom, cudaStream_t stream);
+
 /* ---- FP32 router through the hi/lo pair (replaces rr_launch / rr_scalar / rr_small S:856-861, routertail
  * S:5424, rwdl S:5377): out_f32[m, n] = x . hi^T + x . lo^T, FP32 accumulation. ---- */
 int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,

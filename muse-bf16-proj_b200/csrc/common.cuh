@@ -52,6 +52,25 @@ MBP_DEV uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
   return v;
 }
 
+// Bounded wait for an exchange word tagged with epoch e (tag in the upper 32 bits; data and tag arrive in one
+// store).  t0 = 0 on the first call of a thread; after kWaitLimitNs the status word gets MBP_DEV_TIMEOUT_PEER
+// and `dead` stops further waits of the thread (the words are then read as they are).
+MBP_DEV uint64_t wait_tag(const uint64_t* p, uint32_t e, uint64_t& t0, bool& dead) {
+  uint64_t v = ld_relaxed_sys_u64(p);
+  while ((uint32_t)(v >> 32) != e && !dead) {
+    const uint64_t now = globaltimer();
+    if (t0 == 0) {
+      t0 = now;
+    } else if (now - t0 > kWaitLimitNs) {
+      set_status(MBP_DEV_TIMEOUT_PEER);
+      dead = true;
+    }
+    __nanosleep(32);
+    v = ld_relaxed_sys_u64(p);
+  }
+  return v;
+}
+
 // ------------------------------------------------------------------------------------------------------------
 // shared memory / mbarrier
 // ------------------------------------------------------------------------------------------------------------

@@ -55,6 +55,12 @@ struct __align__(64) GemvParams {
   // (tk, row) = one f32.  A word and its tag travel in one 64-bit store, so a reader needs no fence.
   const int* epoch;
   long long parity_stride;
+  // Fused receive (tagged kinds with `rout` set): this rank's exchange buffer, the projection output [m][rn], the
+  // rank count, and the epoch counter (MBP_TP_COUNTER_SLOTS slots + ticket) the grid's last CTA advances.
+  const uint8_t* rbuf;
+  void* rout;
+  int* ctr;
+  int rn, rP;
   int nout;
   int C;     // 64-column chunks (k / 64)
   int Rout;  // 16-row tiles computed (n_out / 16)
@@ -159,6 +165,76 @@ MBP_DEV void emit_tagged(const GemvParams& p, float4 v, int row, int tk, uint32_
         st_relaxed_sys_u64(out + (size_t)(tk + 1) * p.ldo + row + 8, tag | __float_as_uint(v.w));
       }
     }
+  }
+}
+
+// Fused receive of one CTA: the tiles this CTA computed (row tiles r0 .. r0+rvalid-1, tokens tok0 .. of this
+// token block), as every rank computed them, from this rank's exchange buffer into the output.  Items are split
+// over i0, i0 + istride, ... (the cluster's CTAs share them).
+//   gather (column-parallel): item (q, rr, t) = 8 words of rank q's shard -> 16 BF16 of out row t, columns
+//                             q*ns + (r0+rr)*16 .. +15 (ns = this shard's rows);
+//   sum (row-parallel):       item (rr, t, quad) = 4 consecutive rows, the P ranks' FP32 partials added in rank
+//                             order -> 4 BF16.
+template <int OUTK, int TOK>
+MBP_DEV void tp_receive(const GemvParams& p, uint32_t epoch, int r0, int rvalid, int tok0, int i0, int istride) {
+  const uint64_t* words = reinterpret_cast<const uint64_t*>(p.rbuf + (long long)(epoch & 1u) * p.parity_stride);
+  const int ntok = min(TOK, p.m - tok0);
+  if (ntok <= 0 || rvalid <= 0) return;
+  uint64_t t0 = 0;
+  bool dead = false;
+  if constexpr (OUTK == MBP_OUT_TAGGED_BF16X2) {
+    const int ns = p.Rout * 16, half = p.rn / 2, per_q = rvalid * ntok;
+    for (int it = i0; it < p.rP * per_q; it += istride) {
+      const int q = it / per_q, rest = it - q * per_q, rr = rest / ntok, t = tok0 + rest - rr * ntok;
+      const uint64_t* w = words + (size_t)t * half + q * (ns / 2) + (r0 + rr) * 8;
+      uint32_t d[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) d[g] = (uint32_t)wait_tag(w + g, epoch, t0, dead);
+      uint4 lo, hi;
+      lo.x = (d[0] & 0xffffu) | d[1] << 16;
+      lo.y = (d[2] & 0xffffu) | d[3] << 16;
+      lo.z = (d[4] & 0xffffu) | d[5] << 16;
+      lo.w = (d[6] & 0xffffu) | d[7] << 16;
+      hi.x = (d[0] >> 16) | (d[1] & 0xffff0000u);
+      hi.y = (d[2] >> 16) | (d[3] & 0xffff0000u);
+      hi.z = (d[4] >> 16) | (d[5] & 0xffff0000u);
+      hi.w = (d[6] >> 16) | (d[7] & 0xffff0000u);
+      uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.rout) + (size_t)t * p.rn + q * ns + (r0 + rr) * 16);
+      o[0] = lo;
+      o[1] = hi;
+    }
+  } else {
+    const int per_r = ntok * 4;
+    for (int it = i0; it < rvalid * per_r; it += istride) {
+      const int rr = it / per_r, rest = it - rr * per_r, t = tok0 + (rest >> 2), row = (r0 + rr) * 16 + (rest & 3) * 4;
+      float a[4];
+      for (int q = 0; q < p.rP; ++q) {
+        const uint64_t* w = words + ((size_t)q * p.m + t) * p.rn + row;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float f = __uint_as_float((uint32_t)wait_tag(w + j, epoch, t0, dead));
+          a[j] = q == 0 ? f : a[j] + f;
+        }
+      }
+      *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.rout) + (size_t)t * p.rn + row) =
+          make_uint2(bf16x2_bits(a[0], a[1]), bf16x2_bits(a[2], a[3]));
+    }
+  }
+}
+
+// The grid's last CTA (ticket = grid size - 1) advances the exchange epoch: every CTA read it before taking its
+// ticket, and the next kernel reads it only after this grid has completed.
+// (No static shared memory: the kernels take the whole dynamic allowance; a barrier with predicate broadcasts.)
+MBP_DEV void tp_advance_epoch(int* ctr, int tid) {
+  __syncthreads();
+  int mine = 0;
+  if (tid == 0) {
+    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+    mine = atomicAdd(reinterpret_cast<unsigned*>(ctr + MBP_TP_COUNTER_SLOTS), 1u) == total - 1;
+  }
+  if (__syncthreads_or(mine)) {
+    if (tid < MBP_TP_COUNTER_SLOTS) ctr[tid] += 1;
+    if (tid == 0) ctr[MBP_TP_COUNTER_SLOTS] = 0;
   }
 }
 
@@ -508,36 +584,43 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
     } else {
       for (int idx = tid; idx < NI; idx += nthr) emit(idx, red_item(idx));
     }
-    return;
-  }
-  const uint32_t rank = cluster_rank();
-  const int per = (NI + p.split - 1) / p.split;
-  float4* recv = red + (size_t)(p.wki > 1 ? p.wki : 0) * NI;  // [split][per]: this CTA's slots, after `red`
-  const uint32_t recv_u32 = smem_u32(recv);
-  auto push = [&](int idx, float4 v) {
-    const int o = idx / per;
-    st_dsmem_f4(mapa(recv_u32 + (uint32_t)((int)rank * per + idx - o * per) * 16u, (uint32_t)o), v);
-  };
-  cluster_sync();  // every CTA of the cluster is past its main loop: the slots may be written
-  if (p.wki == 1) {
-    if (warp < nwc) {
-#pragma unroll
-      for (int j = 0; j < RTW; ++j)
-#pragma unroll
-        for (int n = 0; n < MT; ++n) push(((wr * RTW + j) * MT + n) * 32 + lane, acc_item(j, n));
-    }
   } else {
-    for (int idx = tid; idx < NI; idx += nthr) push(idx, red_item(idx));
-  }
-  cluster_sync();  // every push has landed (release / acquire at cluster scope)
-  const int i0 = (int)rank * per, i1 = min(NI, i0 + per);
-  for (int idx = i0 + tid; idx < i1; idx += nthr) {
-    float4 v = recv[idx - i0];
-    for (int q = 1; q < p.split; ++q) {
-      const float4 w = recv[(size_t)q * per + idx - i0];
-      v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+    const uint32_t rank = cluster_rank();
+    const int per = (NI + p.split - 1) / p.split;
+    float4* recv = red + (size_t)(p.wki > 1 ? p.wki : 0) * NI;  // [split][per]: this CTA's slots, after `red`
+    const uint32_t recv_u32 = smem_u32(recv);
+    auto push = [&](int idx, float4 v) {
+      const int o = idx / per;
+      st_dsmem_f4(mapa(recv_u32 + (uint32_t)((int)rank * per + idx - o * per) * 16u, (uint32_t)o), v);
+    };
+    cluster_sync();  // every CTA of the cluster is past its main loop: the slots may be written
+    if (p.wki == 1) {
+      if (warp < nwc) {
+#pragma unroll
+        for (int j = 0; j < RTW; ++j)
+#pragma unroll
+          for (int n = 0; n < MT; ++n) push(((wr * RTW + j) * MT + n) * 32 + lane, acc_item(j, n));
+      }
+    } else {
+      for (int idx = tid; idx < NI; idx += nthr) push(idx, red_item(idx));
     }
-    emit(idx, v);
+    cluster_sync();  // every push has landed (release / acquire at cluster scope)
+    const int i0 = (int)rank * per, i1 = min(NI, i0 + per);
+    for (int idx = i0 + tid; idx < i1; idx += nthr) {
+      float4 v = recv[idx - i0];
+      for (int q = 1; q < p.split; ++q) {
+        const float4 w = recv[(size_t)q * per + idx - i0];
+        v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+      }
+      emit(idx, v);
+    }
+  }
+  if constexpr (OUTK >= MBP_OUT_TAGGED_BF16X2) {
+    if (p.rout) {  // fused receive: this CTA's tiles from every rank, then the epoch ticket
+      const int crank = p.split > 1 ? (int)cluster_rank() : 0;
+      tp_receive<OUTK, TOK>(p, epoch, r0, rvalid, tok0, crank * nthr + tid, nthr * p.split);
+      tp_advance_epoch(p.ctr, tid);
+    }
   }
 }
 
@@ -822,10 +905,17 @@ int plan_impl(int fmt, int Rout, int C, int m, bool f32, int esc, mbp_gemv_geom*
   return rc;
 }
 
+struct RecvArgs {  // fused receive of a tensor-parallel exchange (mbp_gemv_c12_tp)
+  const uint8_t* buf;
+  void* out;
+  int* ctr;
+  int n, P;
+};
+
 int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* esc_off, const uint32_t* esc,
            int esc_cls, int C, int K, int n_out, const uint16_t* x, int ldx, int m, void* const* outs, int nout,
            int ldo, bool f32, const mbp_gemv_geom* geom, cudaStream_t stream, const int* epoch = nullptr,
-           long long parity_stride = 0, int tagged = 0) {
+           long long parity_stride = 0, int tagged = 0, const RecvArgs* recv = nullptr) {
   if (m < 1) return MBP_ERR_M;
   if (!outs || nout < 1 || nout > kMaxOuts) return MBP_ERR_ARG;
   if (parity_stride < 0 || (parity_stride & 15)) return MBP_ERR_ALIGN;
@@ -855,6 +945,9 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   if (rows_w * g.wki > kMaxConsumerWarps) return MBP_ERR_SPLIT;
   const int nblk = g.nblk > 0 ? g.nblk : (Rout + g.rb - 1) / g.rb;
   if (nblk > Rout || (Rout + nblk - 1) / nblk > g.rb) return MBP_ERR_SPLIT;  // a block holds at most rb tiles
+  // A fused receive waits for other ranks' CTAs of the same index: the whole grid must be resident at once
+  // (one CTA per SM).
+  if (recv && (long long)nblk * g.split * ((m + tok - 1) / tok) > sm_count()) return MBP_ERR_SPLIT;
   const Layout L = make_layout(fmt, mt, g.rb, rtw, g.wki, g.kci, g.stages, with_esc);
   if (smem_request(L) > kMaxSmem) return MBP_ERR_SMEM;
   const KernelFn fn = pick(fmt, mt, rtw, tagged ? tagged : f32 ? MBP_OUT_F32 : MBP_OUT_BF16);
@@ -871,6 +964,11 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   for (int o = 0; o < kMaxOuts; ++o) p.outs[o] = o < nout ? outs[o] : nullptr;
   p.epoch = epoch;
   p.parity_stride = epoch ? parity_stride : 0;
+  p.rbuf = recv ? recv->buf : nullptr;
+  p.rout = recv ? recv->out : nullptr;
+  p.ctr = recv ? recv->ctr : nullptr;
+  p.rn = recv ? recv->n : 0;
+  p.rP = recv ? recv->P : 0;
   p.nout = nout;
   p.C = C;
   p.Rout = Rout;
@@ -958,6 +1056,29 @@ int mbp_gemv_c12_multi(const mbp_c12* w, const uint16_t* x, int ldx, int m, int 
   const int tagged = out_kind >= MBP_OUT_TAGGED_BF16X2 ? out_kind : 0;
   return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, esc_class(w->n_esc, w->n, w->k), w->k / 64, w->k,
                 n_out, x, ldx, m, outs, nout, ldo, f32, geom, stream, epoch, parity_stride, tagged);
+}
+
+int mbp_gemv_c12_tp(const mbp_c12* w, const uint16_t* x, int ldx, int m, const mbp_tp_exchange* ex, uint16_t* out,
+                    const mbp_gemv_geom* geom, cudaStream_t stream) {
+  if (!w || !w->units || !w->bases || !w->esc_off || !x || !ex || !out || !ex->counter) return MBP_ERR_ARG;
+  if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
+  if (ex->P < 1 || ex->P > kMaxOuts || ex->rank < 0 || ex->rank >= ex->P) return MBP_ERR_SHAPE;
+  if (ex->mode != MBP_TP_GATHER_BF16 && ex->mode != MBP_TP_SUM_F32) return MBP_ERR_ARG;
+  if (w->n % 16 || w->k % 64 || w->k / 64 > 32766) return MBP_ERR_SHAPE;
+  const bool gather = ex->mode == MBP_TP_GATHER_BF16;
+  if (ex->n != (gather ? w->n * ex->P : w->n)) return MBP_ERR_SHAPE;
+  if (m < 1 || m > 32) return MBP_ERR_M;
+  if (((uintptr_t)out & 15u) || (ex->parity_stride & 15) || ex->parity_stride < 0) return MBP_ERR_ALIGN;
+  void* outs[kMaxOuts];
+  const long long off = gather ? (long long)ex->rank * (w->n / 2) * 8 : (long long)ex->rank * m * ex->n * 8;
+  for (int r = 0; r < ex->P; ++r) {
+    if (!ex->bufs[r]) return MBP_ERR_ARG;
+    outs[r] = static_cast<char*>(ex->bufs[r]) + off;
+  }
+  RecvArgs rv{static_cast<const uint8_t*>(ex->bufs[ex->rank]), out, ex->counter, ex->n, ex->P};
+  return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, esc_class(w->n_esc, w->n, w->k), w->k / 64, w->k,
+                w->n, x, ldx, m, outs, ex->P, gather ? ex->n / 2 : ex->n, !gather, geom, stream, ex->counter,
+                ex->parity_stride, gather ? MBP_OUT_TAGGED_BF16X2 : MBP_OUT_TAGGED_F32, &rv);
 }
 
 int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,

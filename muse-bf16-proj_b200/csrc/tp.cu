@@ -96,23 +96,6 @@ __global__ void __launch_bounds__(kSlots) k_tp_barrier(const __grid_constant__ T
   __syncthreads();
 }
 
-// Bounded wait for a tagged word of epoch e (the tag is the upper 32 bits; data and tag arrive in one store).
-MBP_DEV uint64_t wait_tag(const uint64_t* p, uint32_t e, uint64_t& t0, bool& dead) {
-  uint64_t v = ld_relaxed_sys_u64(p);
-  while ((uint32_t)(v >> 32) != e && !dead) {
-    const uint64_t now = globaltimer();
-    if (t0 == 0) {
-      t0 = now;
-    } else if (now - t0 > kWaitLimitNs) {
-      set_status(MBP_DEV_TIMEOUT_PEER);
-      dead = true;
-    }
-    __nanosleep(32);
-    v = ld_relaxed_sys_u64(p);
-  }
-  return v;
-}
-
 // Receive step of a tagged exchange.  Launched as a programmatic dependent of the GEMV that sends this rank's
 // share, so it starts while that GEMV drains; it reads nothing the stream's earlier kernels write except the
 // tagged words, whose tags it checks.  Block b advances epoch slot b when the GEMV has completed; the epoch's

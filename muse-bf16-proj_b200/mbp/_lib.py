@@ -43,6 +43,11 @@ class HiLo(ctypes.Structure):
     _fields_ = [("units", ctypes.c_void_p), ("n", ctypes.c_int32), ("k", ctypes.c_int32)]
 
 
+class TPExchange(ctypes.Structure):  # mirrors mbp_tp_exchange
+    _fields_ = [("bufs", ctypes.c_void_p * 8), ("parity_stride", ctypes.c_longlong), ("counter", ctypes.c_void_p),
+                ("rank", ctypes.c_int), ("P", ctypes.c_int), ("mode", ctypes.c_int), ("n", ctypes.c_int)]
+
+
 class Geom(ctypes.Structure):
     _fields_ = [("rb", ctypes.c_int32), ("rtw", ctypes.c_int32), ("split", ctypes.c_int32),
                 ("wki", ctypes.c_int32), ("kci", ctypes.c_int32), ("stages", ctypes.c_int32),
@@ -79,6 +84,8 @@ SIGNATURES = [
                                 _P, ctypes.c_longlong, ctypes.POINTER(Geom), _P]),
     ("mbp_tp_finish", _I, [ctypes.POINTER(ctypes.c_void_p), _I, _I, _P, _P, ctypes.c_longlong, _I, _I, _I, _P,
                            _P]),
+    ("mbp_gemv_c12_tp", _I, [ctypes.POINTER(C12), _P, _I, _I, ctypes.POINTER(TPExchange), _P, ctypes.POINTER(Geom),
+                             _P]),
     ("mbp_gemm_c12", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
     ("mbp_gemm_c12_f32", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
 ]

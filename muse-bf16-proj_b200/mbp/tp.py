@@ -37,7 +37,7 @@ import torch
 import torch.distributed as dist
 
 from ._lib import (OUT_TAGGED_BF16X2, OUT_TAGGED_F32, TP_BARRIER, TP_COUNTER_SLOTS, TP_GATHER_BF16, TP_SUM_F32,
-                   check, lib)
+                   TPExchange, check, lib)
 from .ops import BASE_TILE, PackedC12, gemm, gemv, pack_c12
 
 GEMV_MAX_M = 32
@@ -79,7 +79,8 @@ class _GroupSync:
     def __init__(self, group=None):
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         self.flags = PeerBuffer(64, group)
-        self.counter = torch.zeros(TP_COUNTER_SLOTS, dtype=torch.int32,
+        # epoch slots + the fused GEMV's grid ticket
+        self.counter = torch.zeros(TP_COUNTER_SLOTS + 1, dtype=torch.int32,
                                    device=torch.device("cuda", torch.cuda.current_device()))
         self.flag_ptrs = (ctypes.c_void_p * self.world)(*self.flags.ptrs)
 
@@ -181,10 +182,13 @@ class TPLinear:
 
     ``transport``: "p2p" stores GEMV results straight into the peers' exchange buffers (one node, every pair of
     GPUs peer-capable), "nccl" runs the GEMV then an NCCL collective, "auto" picks "p2p" when the group spans
-    more than one GPU of this node and NCCL otherwise (the GEMM calls, m > 32, always use NCCL)."""
+    more than one GPU of this node and NCCL otherwise (the GEMM calls, m > 32, always use NCCL).
+    ``fused`` (p2p): one kernel per call (``mbp_gemv_c12_tp``: the GEMV's CTAs also wait for and assemble their
+    tiles from the other ranks); False runs the GEMV and then the separate receive kernel (``mbp_tp_finish``)."""
 
     def __init__(self, w: torch.Tensor, mode: str, group=None, reduce: str = "all", base_mode: int = BASE_TILE,
-                 transport: str = "auto"):
+                 transport: str = "auto", fused: bool = True):
+        self.fused = fused
         self.group = group
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
@@ -214,13 +218,28 @@ class TPLinear:
         self._sync = _group_sync(self.group)
         self._par = -(-per // 256) * 256                                       # parity-1 buffer offset
         self._xbuf = PeerBuffer(2 * self._par, self.group)
+        ex = TPExchange()
+        for r, ptr in enumerate(self._xbuf.ptrs):
+            ex.bufs[r] = ptr
+        ex.parity_stride = self._par
+        ex.counter = self._sync.counter.data_ptr()
+        ex.rank, ex.P, ex.n = p.rank, p.world, p.n
+        ex.mode = TP_GATHER_BF16 if p.mode == "column" else TP_SUM_F32
+        self._ex = ex
 
     def _forward_p2p(self, x: torch.Tensor) -> torch.Tensor:
         p = self.plan
         m = x.shape[0]
+        out = torch.empty((m, p.n), dtype=torch.bfloat16, device=x.device)
+        if self.fused:
+            # one kernel: the shard's GEMV stores into every rank's buffer and each CTA assembles its tiles
+            xp = x.data_ptr() + (0 if p.mode == "column" else p.rank * (p.k // p.world) * 2)
+            check(lib().mbp_gemv_c12_tp(ctypes.byref(self.packed.desc), ctypes.c_void_p(xp), p.k, m,
+                                        ctypes.byref(self._ex), ctypes.c_void_p(out.data_ptr()), None, _stream()),
+                  "mbp_gemv_c12_tp")
+            return out
         buf, sync = self._xbuf, self._sync
         epoch = ctypes.c_void_p(sync.counter.data_ptr())
-        out = torch.empty((m, p.n), dtype=torch.bfloat16, device=x.device)
         if p.mode == "column":
             # this rank's rows [r*ns, (r+1)*ns) are word columns [r*ns/2, (r+1)*ns/2) of every rank's buffer
             ns = p.n // p.world

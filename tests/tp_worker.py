@@ -1,11 +1,12 @@
 """Worker of tests/test_gpu_tp.py: one rank of a tensor-parallel check (launched by torchrun).
 
 column-parallel fused QKV+gate (K=6144, N=14336, all-gather) and row-parallel output
-projection (K=N=6144, all-reduce and reduce-scatter) at M in {1, 8, 32, 256}, through both transports (NCCL
-collectives, and peer stores from the GEMV plus the flag barrier), checked against the FP32 reference of the
-unsharded projection (rtol 1e-2 / atol 1e-2).  The peer-store path is also checked for: identical bits on every
-rank, identical column outputs to the NCCL path (same per-shard GEMV), back-to-back calls alternating the
-exchange buffers, and replay of a captured CUDA graph.  Exits non-zero on any mismatch."""
+projection (K=N=6144, all-reduce and reduce-scatter) at M in {1, 8, 32, 256}, through every transport (NCCL
+collectives; the GEMV's epoch-tagged peer stores with the receive fused into the GEMV, and with the separate
+receive kernel), checked against the FP32 reference of the unsharded projection (rtol 1e-2 / atol 1e-2).  The
+peer-store paths are also checked for: identical bits on every rank, identical column outputs to the NCCL path
+(same per-shard GEMV), identical row outputs of the fused and two-kernel forms, back-to-back calls alternating
+the exchange buffers, and replay of a captured CUDA graph.  Exits non-zero on any mismatch."""
 import datetime
 import os
 import sys
@@ -51,9 +52,10 @@ def main():
     w_o.view(-1)[idx] *= 256
     w_o = w_o.to(torch.bfloat16).cuda()
     layers = {}
-    for tr in ("nccl", "p2p"):
-        layers[tr] = {"column": TPLinear(w_qkv, "column", transport=tr),
-                      "row-all": TPLinear(w_o, "row", reduce="all", transport=tr)}
+    for tr in ("nccl", "p2p", "p2p-two-kernels"):
+        kw = {"transport": "p2p", "fused": False} if tr == "p2p-two-kernels" else {"transport": tr}
+        layers[tr] = {"column": TPLinear(w_qkv, "column", **kw),
+                      "row-all": TPLinear(w_o, "row", reduce="all", **kw)}
     layers["nccl"]["row-scatter"] = TPLinear(w_o, "row", reduce="scatter", transport="nccl")
     if layers["p2p"]["column"].transport != "p2p":
         fail("p2p transport not selected")
@@ -72,11 +74,14 @@ def main():
                 bad, mx = _bad(out, ref)
                 if bad:
                     fail(f"{tr} {name} m={m}: {bad} elements outside tolerance, max err {mx}")
-                if tr == "p2p" and not _same_on_all_ranks(out):
-                    fail(f"p2p {name} m={m}: ranks disagree")
-                if tr == "p2p" and name == "column":
+                if tr.startswith("p2p") and not _same_on_all_ranks(out):
+                    fail(f"{tr} {name} m={m}: ranks disagree")
+                if tr.startswith("p2p") and name == "column":
                     if not torch.equal(out, layers["nccl"]["column"](x)):
-                        fail(f"p2p column m={m}: differs from the NCCL path")
+                        fail(f"{tr} column m={m}: differs from the NCCL path")
+                if tr == "p2p-two-kernels" and m <= 32 and name == "row-all":
+                    if not torch.equal(out, layers["p2p"]["row-all"](x)):
+                        fail(f"row m={m}: the fused and the two-kernel exchange differ")
 
     # 2. back-to-back calls on one stream (the exchange buffers alternate); outputs read before the next call
     col, row = layers["p2p"]["column"], layers["p2p"]["row-all"]
