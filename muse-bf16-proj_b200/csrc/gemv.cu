@@ -945,14 +945,15 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   if (rows_w * g.wki > kMaxConsumerWarps) return MBP_ERR_SPLIT;
   const int nblk = g.nblk > 0 ? g.nblk : (Rout + g.rb - 1) / g.rb;
   if (nblk > Rout || (Rout + nblk - 1) / nblk > g.rb) return MBP_ERR_SPLIT;  // a block holds at most rb tiles
-  // A fused receive waits for other ranks' CTAs of the same index: the whole grid must be resident at once
-  // (one CTA per SM).
-  if (recv && (long long)nblk * g.split * ((m + tok - 1) / tok) > sm_count()) return MBP_ERR_SPLIT;
   const Layout L = make_layout(fmt, mt, g.rb, rtw, g.wki, g.kci, g.stages, with_esc);
   if (smem_request(L) > kMaxSmem) return MBP_ERR_SMEM;
   const KernelFn fn = pick(fmt, mt, rtw, tagged ? tagged : f32 ? MBP_OUT_F32 : MBP_OUT_BF16);
   int rc = ensure_attrs(fn);
   if (rc) return rc;
+  // A fused receive waits for other ranks' CTAs of the same index: the whole grid must be resident at once.
+  if (recv && (long long)nblk * g.split * ((m + tok - 1) / tok) >
+                  max_ctas(fn, g.split, 32 * (rows_w * g.wki + 1), smem_request(L)))
+    return MBP_ERR_SPLIT;
   GemvParams p;
   if (!encode_bf16_2d(&p.xmap, x, (uint64_t)m, (uint64_t)K, (uint64_t)ldx, (uint32_t)tok, 64u,
                       CU_TENSOR_MAP_SWIZZLE_128B))

@@ -16,17 +16,19 @@ collectives in the same order; all of them run on the current CUDA stream, so a 
 graph.  ``TPPlan`` holds the host-side sharding and assembly rules on their own (tested with gloo CPU ranks).
 
 **Peer-store transport** (``transport="p2p"``, the default on one node, used for the GEMV calls m <= 32): instead
-of a GEMV, an NCCL collective and an assembly kernel, the GEMV stores its result straight into every rank's
-exchange buffer over NVLink (``mbp_gemv_c12_multi``; buffers mapped through CUDA IPC, plain stores, no
-multicast) as 64-bit words whose upper half is the exchange's epoch, and one receive kernel (``mbp_tp_finish``,
-launched as a programmatic dependent so it polls while the GEMV drains) waits until every word it needs carries
-the epoch and writes the output: column-parallel, rank r's GEMV writes its column block of the [m, N] output
-into every rank's buffer and the receive kernel unpacks the assembled buffer; row-parallel, rank r writes its
-FP32 partial into slot r of every rank's [P, m, N] buffer and the receive kernel adds the P slots in rank order
-(the same order, hence the same bits, on every rank) into BF16.  A word and its tag arrive in one store, so no
-system-scope fence (several microseconds each) is needed.  Each layer has two exchange buffers, picked by the
-parity of an epoch counter kept in device memory, so back-to-back calls and CUDA-graph replays never write a
-buffer a peer may still be reading.  The GEMM calls (m > 32) and ``reduce="scatter"`` keep the NCCL path.
+of a GEMV, an NCCL collective and an assembly kernel, ONE kernel per call (``mbp_gemv_c12_tp``): the GEMV stores
+its results straight into every rank's exchange buffer over NVLink (buffers mapped through CUDA IPC, plain
+stores, no multicast) as 64-bit words whose upper half is the exchange's epoch, and then each CTA waits until
+the words of its own tiles from every rank carry the epoch and writes them to the output: column-parallel, rank
+r's GEMV writes its column block of the [m, N] output into every rank's buffer and each CTA gathers its tiles'
+columns of all ranks; row-parallel, rank r writes its FP32 partial into slot r of every rank's [P, m, N] buffer
+and each CTA adds its tiles' P slots in rank order (the same order, hence the same bits, on every rank) into
+BF16.  A word and its tag arrive in one store, so no system-scope fence (several microseconds each) is needed.
+Each layer has two exchange buffers, picked by the parity of an epoch counter kept in device memory (the grid's
+last CTA advances it), so back-to-back calls and CUDA-graph replays never write a buffer a peer may still be
+reading.  ``fused=False`` (or a shard geometry whose grid cannot be resident all at once) runs the GEMV
+(``mbp_gemv_c12_multi``) and then a separate receive kernel (``mbp_tp_finish``) over the same words.  The GEMM
+calls (m > 32) and ``reduce="scatter"`` keep the NCCL path.
 """
 from __future__ import annotations
 
@@ -41,6 +43,7 @@ from ._lib import (OUT_TAGGED_BF16X2, OUT_TAGGED_F32, TP_BARRIER, TP_COUNTER_SLO
 from .ops import BASE_TILE, PackedC12, gemm, gemv, pack_c12
 
 GEMV_MAX_M = 32
+_ERR_SPLIT = -3  # MBP_ERR_SPLIT
 
 
 # ---------------- device memory exchanged between the ranks of a node ----------------
@@ -189,6 +192,7 @@ class TPLinear:
     def __init__(self, w: torch.Tensor, mode: str, group=None, reduce: str = "all", base_mode: int = BASE_TILE,
                  transport: str = "auto", fused: bool = True):
         self.fused = fused
+        self._two_kernel_m: set = set()
         self.group = group
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
@@ -231,13 +235,20 @@ class TPLinear:
         p = self.plan
         m = x.shape[0]
         out = torch.empty((m, p.n), dtype=torch.bfloat16, device=x.device)
-        if self.fused:
+        if self.fused and m not in self._two_kernel_m:
             # one kernel: the shard's GEMV stores into every rank's buffer and each CTA assembles its tiles
             xp = x.data_ptr() + (0 if p.mode == "column" else p.rank * (p.k // p.world) * 2)
-            check(lib().mbp_gemv_c12_tp(ctypes.byref(self.packed.desc), ctypes.c_void_p(xp), p.k, m,
-                                        ctypes.byref(self._ex), ctypes.c_void_p(out.data_ptr()), None, _stream()),
-                  "mbp_gemv_c12_tp")
-            return out
+            rc = lib().mbp_gemv_c12_tp(ctypes.byref(self.packed.desc), ctypes.c_void_p(xp), p.k, m,
+                                       ctypes.byref(self._ex), ctypes.c_void_p(out.data_ptr()), None, _stream())
+            if rc != _ERR_SPLIT:
+                check(rc, "mbp_gemv_c12_tp")
+                return out
+            # this shard's geometry cannot have its whole grid resident at once (every rank plans the same
+            # geometry, so every rank takes this branch): the GEMV and the separate receive kernel, which use
+            # the same words, buffers and epochs
+            self._two_kernel_m.add(m)
+        buf, sync = self._xbuf, self._sync
+        epoch = ctypes.c_void_p(sync.counter.data_ptr())
         buf, sync = self._xbuf, self._sync
         epoch = ctypes.c_void_p(sync.counter.data_ptr())
         if p.mode == "column":
