@@ -222,6 +222,14 @@ int mbp_gemv_c12_tp(const mbp_c12* w, const uint16_t* x, int ldx, int m, const m
 int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,
                     cudaStream_t stream);
 
+/* ---- Router consumer (no counterpart in the reference, which stops at the logits): the k largest of each
+ * token's e logits (rows ld floats apart; e <= 1024, k <= min(e, 32)), ids[t][j] in descending logit order (equal
+ * logits: lower index first; NaN below every number), weights[t][j] = softmax over the k selected logits
+ * (renorm = 1) or the full softmax over all e, taken at the selected ones (renorm = 0).  Launched as a
+ * programmatic dependent of the kernel before it (the router GEMV), whose completion it waits for. ---- */
+int mbp_router_topk(const float* logits, int m, int e, int ld, int k, int renorm, float* weights, int32_t* ids,
+                    cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,12 +21,12 @@ import torch
 from . import store
 from ._lib import MbpError, device_status, lib
 from .ops import (BASE_MATRIX, BASE_TILE, PackedC12, PackedHiLo, gemm, gemv, gemv_plan, pack_c12, pack_hilo,
-                  router, unpack_c12)
+                  router, router_topk, unpack_c12)
 from .store import load_packed, save_packed
 
 __all__ = ["Weights", "Config", "Inputs", "prepare", "kernel_fn", "MbpError", "PackedC12", "PackedHiLo", "pack_c12",
            "unpack_c12", "pack_hilo", "gemv", "gemm", "gemv_plan", "router", "device_status", "BASE_MATRIX", "BASE_TILE",
-           "save_packed", "load_packed", "store"]
+           "save_packed", "load_packed", "store", "router_topk", "route"]
 
 LAYERS = ("qkv_gate", "o", "pooler", "unpooler", "router")
 GEMV_MAX_M = 32  # the reference's decode/verify boundary: small-M GEMVs up to 32 tokens (SM_MAX_M, S:252)
@@ -107,3 +107,10 @@ def kernel_fn(data: Inputs, state: dict) -> torch.Tensor:
     if not 0 < n <= p.n or n % 16:
         raise ValueError(f"n={n} must be a multiple of 16 in (0, {p.n}]")
     return gemv(p, x, n_out=n) if x.shape[0] <= GEMV_MAX_M else gemm(p, x, n_out=n)
+
+
+def route(data: Inputs, state: dict, k: int, renorm: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """The router call followed by its consumer: ``kernel_fn`` on the router layer, then each token's k experts
+    (``router_topk``: ids in descending logit order, softmax weights over the selection or the whole row).  Two
+    launches, the second a programmatic dependent of the first."""
+    return router_topk(kernel_fn(data, state), k, renorm)

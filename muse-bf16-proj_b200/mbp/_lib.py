@@ -74,6 +74,7 @@ SIGNATURES = [
     ("mbp_gemv_c12", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, ctypes.POINTER(Geom), _P]),
     ("mbp_gemv_c12_f32", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, ctypes.POINTER(Geom), _P]),
     ("mbp_router_hilo", _I, [ctypes.POINTER(HiLo), _P, _I, _P, _I, ctypes.POINTER(Geom), _P]),
+    ("mbp_router_topk", _I, [_P, _I, _I, _I, _I, _I, _P, _P, _P]),
     ("mbp_tp_assemble_columns", _I, [_P, _P, _I, _I, _I, _P]),
     ("mbp_f32_to_bf16", _I, [_P, _P, ctypes.c_longlong, _P]),
     ("mbp_ipc_alloc", _I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _P]),

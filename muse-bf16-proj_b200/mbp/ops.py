@@ -187,3 +187,16 @@ def router(p: PackedHiLo, x: torch.Tensor, out: torch.Tensor | None = None, geom
     check(lib().mbp_router_hilo(ctypes.byref(p.desc), _ptr(x), m, _ptr(out), out.stride(0),
                                 ctypes.byref(geom) if geom is not None else None, _stream()), "mbp_router_hilo")
     return out
+
+
+def router_topk(logits: torch.Tensor, k: int, renorm: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """(weights f32 [m, k], ids int32 [m, k]): each row's k largest logits in descending order (equal logits:
+    lower index first) and their softmax weights over the selection (renorm) or over the whole row."""
+    if logits.dim() != 2 or logits.dtype != torch.float32 or not logits.is_cuda or logits.stride(1) != 1:
+        raise ValueError("logits must be a CUDA float32 [m, e] tensor with unit column stride")
+    m, e = logits.shape
+    w = torch.empty((m, k), dtype=torch.float32, device=logits.device)
+    ids = torch.empty((m, k), dtype=torch.int32, device=logits.device)
+    check(lib().mbp_router_topk(_ptr(logits), m, e, logits.stride(0), k, int(bool(renorm)), _ptr(w), _ptr(ids),
+                                _stream()), "mbp_router_topk")
+    return w, ids

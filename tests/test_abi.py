@@ -141,3 +141,17 @@ def test_exchange_entry_points_validate_without_device():
     assert L.mbp_tp_finish(flags, 0, 2, ctypes.c_void_p(64), None, 0, 9, 1, 16, None, None) == -1
     assert L.mbp_tp_finish(flags, 0, 2, ctypes.c_void_p(64), ctypes.c_void_p(16), 0, _lib.TP_GATHER_BF16, 1, 20,
                            ctypes.c_void_p(16), None) == -2
+
+
+def test_router_topk_validates_without_device():
+    from mbp import _lib
+    L = _lib.lib()
+    p = ctypes.c_void_p(16)
+    assert L.mbp_router_topk(None, 1, 256, 256, 8, 1, p, p, None) == -1
+    assert L.mbp_router_topk(p, 0, 256, 256, 8, 1, p, p, None) == -5
+    assert L.mbp_router_topk(p, 1, 256, 256, 33, 1, p, p, None) == -2   # k above 32
+    assert L.mbp_router_topk(p, 1, 4, 4, 8, 1, p, p, None) == -2        # k above e
+    assert L.mbp_router_topk(p, 1, 2048, 2048, 8, 1, p, p, None) == -2  # e above 1024
+    assert L.mbp_router_topk(p, 1, 256, 128, 8, 1, p, p, None) == -2    # row stride below e
+    assert L.mbp_router_topk(p, 1, 256, 256, 8, 2, p, p, None) == -1    # renorm flag
+    assert L.mbp_router_topk(ctypes.c_void_p(18), 1, 256, 256, 8, 1, p, p, None) == -4

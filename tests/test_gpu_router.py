@@ -54,3 +54,49 @@ def test_router_through_api():
     assert out.dtype == torch.float32 and out.shape == (8, 256)
     ref = x.double() @ w.double().T
     assert float((out.double() - ref).norm() / ref.norm()) <= 1e-5
+
+
+def _topk_reference(logits: torch.Tensor, k: int, renorm: bool):
+    """Row-wise: ids by (value descending, index ascending), NaN below every number; softmax in float64."""
+    lg = logits.double().cpu()
+    key = torch.where(torch.isnan(lg), torch.full_like(lg, float("-inf")), lg)
+    ids, ws = [], []
+    for row in key:
+        order = sorted(range(row.numel()), key=lambda c: (-float(row[c]), c))[:k]
+        sel = row[order]
+        top = float(sel[0])
+        ex = torch.exp(sel - top)
+        den = ex.sum() if renorm else torch.exp(row - top).sum()
+        ids.append(order)
+        ws.append((ex / den).tolist())
+    return torch.tensor(ws, dtype=torch.float64), torch.tensor(ids, dtype=torch.int32)
+
+
+@pytest.mark.parametrize("m,e,k", [(1, 256, 8), (8, 256, 1), (33, 256, 2), (256, 256, 8), (5, 100, 32),
+                                   (3, 1024, 4), (17, 64, 64 // 2)])
+@pytest.mark.parametrize("renorm", [True, False])
+def test_router_topk(m, e, k, renorm):
+    import mbp
+    g = torch.Generator().manual_seed(m * 1000 + e + k)
+    logits = torch.randn(m, e, generator=g) * 3
+    logits[0, : e // 4] = torch.round(logits[0, : e // 4])  # ties: lower index first
+    if m > 2:
+        logits[2, 5] = float("nan")
+    w, ids = mbp.router_topk(logits.cuda(), k, renorm)
+    rw, rids = _topk_reference(logits, k, renorm)
+    assert torch.equal(ids.cpu(), rids)
+    assert torch.allclose(w.cpu().double(), rw, rtol=1e-5, atol=1e-7)
+    assert mbp.device_status() == 0
+
+
+def test_route_on_prepared_router():
+    import mbp
+    g = torch.Generator().manual_seed(21)
+    wr = (torch.randn(256, 6144, generator=g) * 0.01).cuda()
+    st = mbp.prepare({"router": wr})
+    x = (torch.randn(32, 6144, generator=g)).to(torch.bfloat16).cuda()
+    data = {"x": x, "config": {"m": 32, "n": 256, "k": 6144, "layer": "router"}}
+    w, ids = mbp.route(data, st, 8)
+    w2, ids2 = mbp.router_topk(mbp.kernel_fn(data, st), 8)
+    assert torch.equal(ids, ids2) and torch.equal(w, w2)
+    assert torch.allclose(w.sum(1), torch.ones(32, device="cuda"), atol=1e-6)
