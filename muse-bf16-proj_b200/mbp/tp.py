@@ -101,7 +101,7 @@ class _GroupSync:
 
 def _same_node(group) -> bool:
     """True when every rank of `group` drives a different GPU of this host and all pairs are peer-capable (the
-    barrier's spin waits need the ranks on separate GPUs running concurrently)."""
+    exchange's waits need the ranks on separate GPUs running concurrently)."""
     import socket
     world = dist.get_world_size(group)
     dev = torch.cuda.current_device()
