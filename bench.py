@@ -499,7 +499,8 @@ def run_mbp_tp(args, rank, world):
             "data": "synthetic: W~N(0,0.02) torch seed 0 (+1% x256 variant, randperm seed 2), x~N(0,1) seed 1",
             "config": {"workload": "config2 decode GEMV step (16 calls), tensor-parallel: qkv_gate column-parallel + "
                                    "all-gather, o row-parallel + all-reduce of FP32 partials",
-                       "transport": ("GEMV peer stores over NVLink (CUDA IPC) + flag barrier/assemble kernel"
+                       "transport": ("one kernel per call: the shard GEMV stores epoch-tagged words into every "
+                                     "rank's buffer over NVLink (CUDA IPC) and its CTAs assemble their tiles"
                                      if transport == "p2p" else "NCCL collectives"),
                        "l2": "cold by construction (>=250 MB of other weights between reuses of a matrix on one GPU "
                              "at N=1; per-GPU shards at N>1)",
