@@ -15,8 +15,12 @@
 //     shared loads first (instruction-level parallelism across units), decodes each 1536-byte unit in registers
 //     (3 prmt per 8 weights), patches escapes through an unbounded per-tile list (escape.cuh) and issues 4*MT
 //     mma.sync per unit into several independent accumulators;
-//   * split-K: the wki K slices reduce through shared memory, the `split` CTAs of a thread-block cluster through
-//     distributed shared memory, each rank reducing and storing 1/split of the tile;
+//   * split-K: the wki K slices reduce through shared memory, the `split` CTAs of a thread-block cluster push
+//     their partials into the owning CTA through distributed shared memory, each rank summing and storing
+//     1/split of the tile; without a K split every warp stores its sums straight from registers;
+//   * tensor-parallel exchange (output kinds MBP_OUT_TAGGED_*): the results go to every rank's exchange buffer as
+//     epoch-tagged 64-bit words over NVLink, and with a fused receive each CTA then gathers (or sums, in rank
+//     order) its tiles from every rank into the output, the grid's last CTA advancing the epoch;
 //   * every wait is bounded and reports through the device status word (no trap).
 //
 // The same kernel serves the FP32 router (S:854, S:941, S:943, S:5377, S:5424) with hi/lo BF16 units: two

@@ -8,7 +8,9 @@
 // Peer-store exchange (one node, NVLink peers mapped through CUDA IPC; plain loads and stores, no multicast):
 //   mbp_ipc_alloc / mbp_ipc_open / mbp_ipc_close / mbp_ipc_free   exchange buffers and their cross-process
 //                            mappings
-//   mbp_tp_finish            the receive step.  The sending GEMVs (mbp_gemv_c12_multi, tagged outputs) store
+//   mbp_tp_finish            the receive step of the two-kernel form (the one-kernel form, mbp_gemv_c12_tp,
+//                            does the same inside the GEMV).  The sending GEMVs (mbp_gemv_c12_multi, tagged
+//                            outputs) store
 //                            64-bit words that carry the exchange's epoch in their upper half into every rank's
 //                            buffer; the receive kernel polls its own buffer until each word it needs carries
 //                            the epoch, then writes the assembled BF16 columns, or the rank-order sum of the P
