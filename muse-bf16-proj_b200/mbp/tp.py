@@ -53,6 +53,7 @@ class PeerBuffer:
     r's buffer as seen from this process."""
 
     def __init__(self, nbytes: int, group=None):
+        self.group, self.nbytes = group, nbytes
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         own = ctypes.c_void_p()
         handle = (ctypes.c_char * 64)()
@@ -73,6 +74,25 @@ class PeerBuffer:
         """Pointers (plus a byte offset) with this rank's first, as a ctypes array for mbp_gemv_c12_multi."""
         order = [self.rank] + [r for r in range(self.world) if r != self.rank]
         return (ctypes.c_void_p * self.world)(*[self.ptrs[r] + offset for r in order])
+
+    @property
+    def closed(self) -> bool:
+        return self.own is None
+
+    def close(self):
+        """Collective over the group (every rank calls it, in the same order as its other collectives): waits for
+        this device's queued work, unmaps the peers' buffers once every rank has got that far, and frees this
+        rank's own buffer once every rank has unmapped it.  A second call does nothing."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)        # no rank's kernels still store into or read from any buffer
+        for r, ptr in enumerate(self.ptrs):
+            if r != self.rank:
+                check(lib().mbp_ipc_close(ctypes.c_void_p(ptr)), "mbp_ipc_close")
+        dist.barrier(group=self.group)        # every peer mapping of this rank's buffer is gone
+        own, self.own, self.ptrs = self.own, None, []
+        check(lib().mbp_ipc_free(ctypes.c_void_p(own)), "mbp_ipc_free")
 
 
 class _GroupSync:
@@ -98,6 +118,10 @@ class _GroupSync:
         """Flag barrier of the group on the current stream (orders every rank's earlier stores before it)."""
         self.finish(None, 0, TP_BARRIER, 0, 0, None)
 
+    def close(self):
+        """Collective: releases the flag arrays (see ``PeerBuffer.close``)."""
+        self.flags.close()
+
 
 def _same_node(group) -> bool:
     """True when every rank of `group` drives a different GPU of this host and all pairs are peer-capable (the
@@ -121,8 +145,12 @@ def _same_node(group) -> bool:
 _SYNCS: dict = {}
 
 
+def _sync_key(group):
+    return id(group) if group is not None else None
+
+
 def _group_sync(group) -> _GroupSync:
-    key = id(group) if group is not None else None
+    key = _sync_key(group)
     if key not in _SYNCS:
         _SYNCS[key] = _GroupSync(group)
     return _SYNCS[key]
@@ -249,8 +277,6 @@ class TPLinear:
             self._two_kernel_m.add(m)
         buf, sync = self._xbuf, self._sync
         epoch = ctypes.c_void_p(sync.counter.data_ptr())
-        buf, sync = self._xbuf, self._sync
-        epoch = ctypes.c_void_p(sync.counter.data_ptr())
         if p.mode == "column":
             # this rank's rows [r*ns, (r+1)*ns) are word columns [r*ns/2, (r+1)*ns/2) of every rank's buffer
             ns = p.n // p.world
@@ -274,7 +300,16 @@ class TPLinear:
             return gemv(self.packed, xs, out_dtype=out_dtype)
         return gemm(self.packed, xs, out_dtype=out_dtype)
 
+    def close(self):
+        """Collective over the group: releases this layer's exchange buffers and packed shard; later calls raise.
+        The group's flag arrays and epoch slots stay (other layers share them; ``release_tp`` drops them)."""
+        if self._xbuf is not None:
+            self._xbuf.close()
+        self._xbuf, self.packed = None, None
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.packed is None:
+            raise RuntimeError("TPLinear used after close()")
         p = self.plan
         m = x.shape[0]
         if self._xbuf is not None and 1 <= m <= GEMV_MAX_M and (p.mode == "column" or self.reduce == "all"):
@@ -325,6 +360,23 @@ def prepare_tp(weights: dict, group=None, modes: dict | None = None, reduce: str
     modes = dict(DEFAULT_MODES if modes is None else modes)
     return {"tp": {name: TPLinear(w, modes.get(name, "column"), group, reduce, transport=transport)
                    for name, w in weights.items()}}
+
+
+def release_tp(state: dict):
+    """Collective teardown of ``prepare_tp``'s state (every rank of the layers' group calls it with the state it
+    prepared): closes every layer in name order, then the flag arrays and epoch slots of the groups those layers
+    exchanged over (in the order the names first reach them, the same on every rank)."""
+    layers = state.get("tp", {})
+    keys = []
+    for name in sorted(layers):
+        layer = layers[name]
+        if layer._xbuf is not None and _sync_key(layer.group) not in keys:
+            keys.append(_sync_key(layer.group))
+        layer.close()
+    for key in keys:
+        sync = _SYNCS.pop(key, None)
+        if sync is not None:
+            sync.close()
 
 
 def kernel_fn_tp(data: dict, state: dict) -> torch.Tensor:

@@ -38,7 +38,7 @@ def main():
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60))
     import mbp
-    from mbp.tp import TPLinear
+    from mbp.tp import TPLinear, release_tp
     fails = []
 
     def fail(msg):
@@ -131,6 +131,22 @@ def main():
     torch.cuda.synchronize()
     if mbp.device_status() != 0:
         fail("device status set")
+
+    # 4. collective teardown: the exchange buffers (cudaMalloc'd outside torch's cache) go back to the device and
+    # a released layer refuses further calls
+    xbytes = sum(lin._xbuf.nbytes for ls in layers.values() for lin in ls.values() if lin._xbuf is not None)
+    free0 = torch.cuda.mem_get_info()[0]
+    for tr in ("nccl", "p2p", "p2p-two-kernels"):
+        release_tp({"tp": layers[tr]})
+    torch.cuda.synchronize()
+    freed = torch.cuda.mem_get_info()[0] - free0
+    if freed < xbytes // 2:
+        fail(f"teardown freed {freed} bytes of {xbytes} exchange bytes")
+    try:
+        col(xs[0])
+        fail("a released layer accepted a call")
+    except RuntimeError:
+        pass
     flag = torch.tensor([1 if fails else 0], device="cuda")
     dist.all_reduce(flag)
     dist.destroy_process_group()
