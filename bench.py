@@ -1,15 +1,15 @@
-"""Benchmark of the small-M projection on B200 (BASELINE.json config 2 at N=1).
+"""Benchmark of the small-M projection on B200 (the decode configuration at N=1).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mbp|reference]
 
-Workload (one STEP): one call of each decode-GEMV shape of BASELINE config 2 -- fused QKV+gate (K=6144,
+Workload (one STEP): one call of each decode-GEMV shape -- fused QKV+gate (K=6144,
 N=14336) and O (K=N=6144) at M in {1, 8, 16, 32} -- with plain N(0, 0.02) weights and with the 1%-x256 escape
 variant: 16 calls.  The calls are ordered M-major over the four matrices (qkv, o, qkv-escape, o-escape), so
 between two uses of one matrix at least 250 MB of other weights stream through the 126 MB L2: every call
 reads its weights cold (inputs larger than L2; no flush kernel).  The step is captured once as a CUDA graph and
 replayed (the reference's judge also timed graph replays).
 
-value      = packed weight bytes of a step / device time of a step (TB/s): the BASELINE metric's bandwidth
+value      = packed weight bytes of a step / device time of a step (TB/s): the headline metric's bandwidth
              form; per-shape us/call (graph replay over rotating copies of that matrix) are under "shapes".
 e2e        = the same step through the public API (mbp.kernel_fn) from pinned host buffers: H2D of x, the call
              (new output tensor each call), D2H of the output, all inside the timed region.
@@ -364,9 +364,9 @@ def run_mbp(args, rank, world):
 
 
 def run_mbp_tp(args, rank, world):
-    """N > 1: the same 16-call step, each projection tensor-parallel over the N ranks (BASELINE config 5 layout:
-    QKV+gate column-parallel + all-gather, O row-parallel + all-reduce of FP32 partials; by default through the
-    GEMV's peer stores and the receive kernel, `--transport nccl` for NCCL collectives).  Total work is fixed
+    """N > 1: the same 16-call step, each projection tensor-parallel over the N ranks (QKV+gate column-parallel
+    + all-gather, O row-parallel + all-reduce of FP32 partials; by default through the GEMV's peer stores with
+    the receive fused into it, `--transport nccl` for NCCL collectives).  Total work is fixed
     (strong scaling); value = packed bytes of the unsharded layers per step / step time (max over ranks)."""
     import torch
     import torch.distributed as dist

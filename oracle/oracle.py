@@ -2,7 +2,7 @@
 
 TEST INFRASTRUCTURE ONLY: used by tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline legs as the
 checker.  The numpy restatement in ``c12.py`` is the readable oracle; this module is its fast twin for
-BASELINE-sized matrices, and ``tests/test_oracle_c.py`` checks that the two agree bit for bit.
+full-size matrices (up to 14336 x 6144), and ``tests/test_oracle_c.py`` checks that the two agree bit for bit.
 """
 from __future__ import annotations
 

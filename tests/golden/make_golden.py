@@ -89,7 +89,7 @@ def main():
     assert ref.SM_SIGN_POS == (3, 19, 7, 23, 11, 27, 15, 31)
     summary = {"generator": "tests/golden/make_golden.py", "cases": {}}
 
-    # 1. small N(0, 0.02) matrix, the BASELINE distribution
+    # 1. small N(0, 0.02) matrix, the benchmark's weight distribution
     torch.manual_seed(0)
     w = (torch.randn(64, 256) * 0.02).to(torch.bfloat16)
     case = packed_case(ref, w)
@@ -99,7 +99,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "c12_n64_k256.npz"), **case)
     summary["cases"]["c12_n64_k256"] = {"base": int(case["base"]), "n_esc": int(case["esc_r"].size)}
 
-    # 2. escape stress: 1% of weights scaled x256 (the BASELINE escape variant, small)
+    # 2. escape stress: 1% of weights scaled x256 (the benchmark's escape variant, small)
     torch.manual_seed(0)
     w = (torch.randn(32, 512) * 0.02)
     idx = torch.randperm(w.numel(), generator=torch.Generator().manual_seed(2))[: w.numel() // 100]
@@ -136,7 +136,7 @@ def main():
                         data=pk["data"].numpy().astype(np.uint8),
                         exact=ref.sm_exact(wr, 2).numpy(), x0=xs[0], x1=xs[1], ref0=refs[0], ref1=refs[1])
 
-    # 5. known answers on the BASELINE config-1 matrix (4096 x 4096, N(0, 0.02), torch seed 0): too large to
+    # 5. known answers on the reference's CPU-runnable matrix (4096 x 4096, N(0, 0.02), torch seed 0): too large to
     #    store, so the fixture keeps the reference's base, escape count and sha256 of its packed bytes.
     torch.manual_seed(0)
     w = (torch.randn(4096, 4096) * 0.02).to(torch.bfloat16)

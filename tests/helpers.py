@@ -1,4 +1,5 @@
-"""Shared helpers for the GPU parity tests: seeded inputs (BASELINE.json recipes) and comparison rules."""
+"""Shared helpers for the GPU parity tests: seeded inputs (the benchmark's N(0, 0.02) weights, optionally with
+1% of them scaled x256; N(0, 1) tokens) and comparison rules."""
 import numpy as np
 import torch
 
@@ -9,7 +10,7 @@ def bits_np(t: torch.Tensor) -> np.ndarray:
 
 def weight(n, k, seed=0, scale=0.02, escape_frac=0.0, device="cuda"):
     """W = (randn(n, k) * scale) as BF16 (torch seed), optionally with a fraction of weights scaled x256 at
-    positions randperm(n*k, seed 2) -- the BASELINE escape variant."""
+    positions randperm(n*k, seed 2) -- the benchmark's escape variant."""
     g = torch.Generator().manual_seed(seed)
     w = torch.randn(n, k, generator=g) * scale
     if escape_frac:
@@ -24,7 +25,7 @@ def tokens(m, k, seed=1, device="cuda"):
 
 
 def assert_close_bf16(out: torch.Tensor, ref_f32: torch.Tensor, rtol=1e-2, atol=1e-2):
-    """BASELINE tolerance: BF16 outputs within rtol 1e-2 / atol 1e-2 of an FP32-accumulated reference."""
+    """The path's tolerance: BF16 outputs within rtol 1e-2 / atol 1e-2 of an FP32-accumulated reference."""
     o = out.float()
     err = (o - ref_f32).abs()
     bound = atol + rtol * ref_f32.abs()

@@ -3,7 +3,7 @@
 * one-hot exactness (the reference's sm_verify_onehot idea, S:281-294): rows of x = e_k reproduce W[:, k] bit
   for bit, which pins the decode into shared memory, the swizzled operand layout, the UMMA descriptors and the
   TMEM epilogue mapping;
-* BASELINE config 3 shapes (M in {128, 256}; QKV+gate, O, pooler 6144->1536, unpooler 1536->6144) against the
+* the prefill shapes (M in {128, 256}; QKV+gate, O, pooler 6144->1536, unpooler 1536->6144) against the
   FP32 reference at rtol 1e-2 / atol 1e-2 plus the reference's norm rule (S:297-317);
 * ragged token counts (tiles of up to 256 tokens, token tails), n_out < n, escape-heavy weights, FP32 output.
 """

@@ -2,10 +2,10 @@
 
 * one-hot exactness (the reference's sm_verify_onehot, S:281-294): x = e_k rows must reproduce W[:, k] bit for
   bit, which pins decode, escape patching, fragment mapping and output indexing;
-* random inputs against the oracle (C port, sampled rows) and an FP32 reference, BASELINE tolerance
+* random inputs against the oracle (C port, sampled rows) and an FP32 reference, tolerance
   rtol 1e-2 / atol 1e-2, plus the reference's own norm rule (S:297-317);
-* BASELINE config-2 shapes M in {1, 8, 16, 32} with and without the 1% x256 escape variant, every token count
-  1..33 on a small matrix, M > 32 (token blocks), n_out < n (the reference's unpooler n=1024), FP32 output.
+* the decode shapes (QKV+gate 6144->14336, O 6144->6144) at M in {1, 8, 16, 32} with and without the 1% x256
+  escape variant, every token count 1..33 on a small matrix, M > 32 (token blocks), n_out < n (the reference's unpooler n=1024), FP32 output.
 """
 import numpy as np
 import pytest
@@ -72,7 +72,7 @@ def test_every_token_count_small(m):
 @pytest.mark.parametrize("m", [1, 8, 16, 32])
 @pytest.mark.parametrize("frac", [0.0, 0.01])
 def test_baseline_config2(shape, m, frac):
-    """BASELINE config 2 against the FP32 reference and the C oracle on a row sample."""
+    """The decode shapes against the FP32 reference and the C oracle on a row sample."""
     import mbp
     w = weight(*shape, seed=0, escape_frac=frac)
     p = mbp.pack_c12(w)

@@ -69,7 +69,7 @@ def test_pack_large_against_c_oracle(shape, frac):
 @pytest.mark.parametrize("shape", [(14336, 6144), (6144, 6144)])
 @pytest.mark.parametrize("frac", [0.0, 0.01])
 def test_round_trip_baseline_shapes(shape, frac):
-    """Full BASELINE shapes: device round trip bit-exact; escape count equals the oracle's count."""
+    """Full benchmark shapes: device round trip bit-exact; escape count equals the oracle's count."""
     import mbp
     w = weight(*shape, seed=0, escape_frac=frac)
     p = mbp.pack_c12(w, mbp.BASE_TILE)

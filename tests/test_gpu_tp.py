@@ -1,4 +1,5 @@
-"""Tensor-parallel projections on 2, 4 and 8 GPUs, through the NCCL and the peer-store
+"""Tensor-parallel projections on 2, 4 and 8 GPUs (column-parallel QKV+gate, row-parallel output projection),
+through the NCCL and the peer-store
 transports; each size is skipped with fewer GPUs.
 
 Runs tests/tp_worker.py under torchrun (rendezvous on 127.0.0.1, NVLS off), bounded by a timeout."""

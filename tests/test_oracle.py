@@ -122,7 +122,7 @@ def test_bf16_rounding():
 
 @pytest.mark.slow
 def test_config1_known_answer():
-    """BASELINE config 1 (4096 x 4096, N(0, 0.02), torch seed 0): the reference's base, escape count and packed
+    """The reference's CPU-runnable case (4096 x 4096, N(0, 0.02), torch seed 0): its base, escape count and packed
     bytes (sha256) are reproduced by the oracle."""
     import torch
     s = json.load(open(os.path.join(GOLDEN, "golden_summary.json")))["config1_4096x4096"]

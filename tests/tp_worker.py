@@ -1,6 +1,6 @@
 """Worker of tests/test_gpu_tp.py: one rank of a tensor-parallel check (launched by torchrun).
 
-column-parallel fused QKV+gate (K=6144, N=14336, all-gather) and row-parallel output
+Column-parallel fused QKV+gate (K=6144, N=14336, all-gather) and row-parallel output
 projection (K=N=6144, all-reduce and reduce-scatter) at M in {1, 8, 32, 256}, through every transport (NCCL
 collectives; the GEMV's epoch-tagged peer stores with the receive fused into the GEMV, and with the separate
 receive kernel), checked against the FP32 reference of the unsharded projection (rtol 1e-2 / atol 1e-2).  The
