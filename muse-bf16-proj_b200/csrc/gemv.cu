@@ -472,8 +472,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
 #pragma unroll
               for (int s = 0; s < MG; ++s) tgt[j][s] = 0u;
               if ((int)cur[j].next_chunk < c0 + gend)
-                cur[j].scatter<MG>((uint32_t)(c0 + g0), (uint32_t)(c0 + gend), xr + (uint32_t)j * kMaskUnitBytes,
-                                   RTW * kMaskUnitBytes, lane, tgt[j]);
+                cur[j].template scatter<MG>((uint32_t)(c0 + g0), (uint32_t)(c0 + gend),
+                                            xr + (uint32_t)j * kMaskUnitBytes, RTW * kMaskUnitBytes, lane, tgt[j]);
             }
             __syncwarp();
           }
@@ -562,17 +562,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
     const int tk = tok0 + n * 8 + 2 * (ln & 3);
     if constexpr (OUTK >= MBP_OUT_TAGGED_BF16X2) {
       emit_tagged<OUTK>(p, v, row, tk, epoch);
-      return;
-    }
-    for (int o = 0; o < p.nout; ++o) {
-      OutT* out = reinterpret_cast<OutT*>(p.outs[o]);
-      if (tk < p.m) {
-        store_out(out + (size_t)tk * p.ldo + row, v.x);
-        store_out(out + (size_t)tk * p.ldo + row + 8, v.z);
-      }
-      if (tk + 1 < p.m) {
-        store_out(out + (size_t)(tk + 1) * p.ldo + row, v.y);
-        store_out(out + (size_t)(tk + 1) * p.ldo + row + 8, v.w);
+    } else {
+      for (int o = 0; o < p.nout; ++o) {
+        OutT* out = reinterpret_cast<OutT*>(p.outs[o]);
+        if (tk < p.m) {
+          store_out(out + (size_t)tk * p.ldo + row, v.x);
+          store_out(out + (size_t)tk * p.ldo + row + 8, v.z);
+        }
+        if (tk + 1 < p.m) {
+          store_out(out + (size_t)(tk + 1) * p.ldo + row, v.y);
+          store_out(out + (size_t)(tk + 1) * p.ldo + row + 8, v.w);
+        }
       }
     }
   };
