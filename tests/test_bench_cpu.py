@@ -1,12 +1,34 @@
-"""bench.py's reference arm on the host: one run of `--impl reference` prints exactly one JSON line with the keys
-the result collector reads (the same metric, unit and direction as the GPU arm, a cpu_baseline describing the run,
-and an e2e object with zero copy bytes)."""
+"""bench.py on the host: the clock-sampling summary that goes into every JSON line, and the reference arm (one run
+of `--impl reference` prints exactly one JSON line with the keys the result collector reads: the same metric,
+unit and direction as the GPU arm, a cpu_baseline describing the run, and an e2e object with zero copy bytes)."""
 import json
 import os
 import subprocess
 import sys
 
 from conftest import ROOT
+
+
+def test_clock_summary_parses_sampled_rows():
+    """The `clocks` object: median SM clock under load, the max clock, and every throttle reason seen Active
+    (the nvidia-smi csv,noheader,nounits rows of the query bench.py issues; malformed rows are skipped)."""
+    import bench
+    c = bench.Clocks(0)
+    rows = ["0, 1965, 1965, 640.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+            "0, 1800, 1965, 990.5, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+            "0, 1890, 1965, 985.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+            "[N/A] garbled line",
+            "0, 1900, 1965, 700.0, 0x0000000000000000, Not Active, Not Active, Active, Not Active"]
+    c.f.write("\n".join(rows) + "\n")
+    s = c.summary()
+    assert s["sm_mhz"] == 1895.0 and s["sm_max_mhz"] == 1965.0 and s["samples"] == 4
+    assert s["reasons"] == ["sw_power_cap", "sw_thermal_slowdown"]
+
+
+def test_clock_summary_without_samples():
+    import bench
+    c = bench.Clocks(0)
+    assert c.summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
 
 
 def test_reference_arm_prints_one_contract_line():
