@@ -123,20 +123,28 @@ class _GroupSync:
         self.flags.close()
 
 
+def _p2p_placement_ok(seen: list, host: str, local: dict, dev: int, can_access) -> bool:
+    """The peer-store rule for one rank: `seen` = (hostname, GPU uuid) of every rank, `local` = uuid -> device
+    index of the GPUs this process sees, `dev` = this rank's device index, `can_access(a, b)` = peer access.
+    True only for at most 8 ranks on this host, each on a GPU of its own (waiting kernels of two ranks on one GPU
+    are not guaranteed to run at the same time), every peer visible here being peer-accessible."""
+    if len(seen) > 8 or len({u for _, u in seen}) != len(seen) or any(h != host for h, _ in seen):
+        return False
+    return all(can_access(dev, local[u]) for _, u in seen if u in local and local[u] != dev)
+
+
 def _same_node(group) -> bool:
     """True when every rank of `group` drives a different GPU of this host and all pairs are peer-capable (the
-    exchange's waits need the ranks on separate GPUs running concurrently)."""
+    exchange's waits need the ranks on separate GPUs running concurrently); every rank must agree."""
     import socket
     world = dist.get_world_size(group)
     dev = torch.cuda.current_device()
     me = (socket.gethostname(), str(torch.cuda.get_device_properties(dev).uuid))
     seen = [None] * world
     dist.all_gather_object(seen, me, group=group)
-    ok = world <= 8 and len({s[1] for s in seen}) == world and all(s[0] == me[0] for s in seen)
-    if ok:
-        # peers visible to this process by uuid (all of them when ranks share the device list)
-        local = {str(torch.cuda.get_device_properties(i).uuid): i for i in range(torch.cuda.device_count())}
-        ok = all(torch.cuda.can_device_access_peer(dev, local[u]) for _, u in seen if u in local and local[u] != dev)
+    # peers visible to this process by uuid (all of them when ranks share the device list)
+    local = {str(torch.cuda.get_device_properties(i).uuid): i for i in range(torch.cuda.device_count())}
+    ok = _p2p_placement_ok([tuple(s) for s in seen], me[0], local, dev, torch.cuda.can_device_access_peer)
     votes = [None] * world
     dist.all_gather_object(votes, ok, group=group)
     return all(votes)

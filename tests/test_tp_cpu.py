@@ -1,7 +1,8 @@
 """Tensor-parallel host logic on CPU ranks (gloo, world size 2): the sharding plan, the collective choreography
 and the output assembly reproduce the unsharded projection; a rank that disappears makes the survivor's
-collective fail within the process-group timeout instead of hanging.  The local products are computed by the CPU
-oracle (each rank packs its own shard with its own exponent bases and escapes), so no GPU is involved."""
+collective fail within the process-group timeout instead of hanging; the peer-store transport is chosen only for
+ranks on GPUs of their own.  The local products are computed by the CPU oracle (each rank packs its own shard with
+its own exponent bases and escapes), so no GPU is involved."""
 import datetime
 import os
 import socket
@@ -138,3 +139,26 @@ def test_plan_rules():
         TPPlan("row", 8, 0, 6144, 6000)
     with pytest.raises(ValueError):
         TPPlan("column", 3, 0, 6144 + 16, 6144)
+
+
+def test_peer_store_placement_rule():
+    """The peer-store transport (kernels that wait on each other's stores) is chosen only when every rank has a
+    GPU of its own on this host, at most 8 ranks, and every visible peer is peer-accessible; anything else falls
+    back to NCCL."""
+    from mbp.tp import _p2p_placement_ok
+    local = {f"GPU-{i}": i for i in range(8)}
+
+    def peers(a, b):
+        return True
+
+    def seen(uuids, hosts=None):
+        return [((hosts or {}).get(i, "h"), u) for i, u in enumerate(uuids)]
+
+    assert _p2p_placement_ok(seen(["GPU-0", "GPU-1"]), "h", local, 0, peers)
+    assert _p2p_placement_ok(seen([f"GPU-{i}" for i in range(8)]), "h", local, 3, peers)
+    assert not _p2p_placement_ok(seen(["GPU-0", "GPU-0"]), "h", local, 0, peers)          # two ranks, one GPU
+    assert not _p2p_placement_ok(seen(["GPU-0", "GPU-1"], {1: "other"}), "h", local, 0, peers)  # two hosts
+    assert not _p2p_placement_ok(seen([f"GPU-{i}" for i in range(9)]), "h", dict(local, **{"GPU-8": 8}), 0, peers)
+    assert not _p2p_placement_ok(seen(["GPU-0", "GPU-1"]), "h", local, 0, lambda a, b: False)  # no peer access
+    # a peer this process cannot see (per-rank device lists) is not asked about
+    assert _p2p_placement_ok(seen(["GPU-0", "GPU-5"]), "h", {"GPU-0": 0}, 0, lambda a, b: False)
