@@ -42,7 +42,7 @@ def _worker_parity(rank, world, port, errq):
     try:
         _setup(rank, world, port)
         from mbp.tp import TPPlan
-        from oracle import c12, oracle
+        from oracle import oracle
         g = torch.Generator().manual_seed(0)
         n, k = 256, 512
         w = (torch.randn(n, k, generator=g) * 0.02)
