@@ -6,7 +6,9 @@ collectives; the GEMV's epoch-tagged peer stores with the receive fused into the
 receive kernel), checked against the FP32 reference of the unsharded projection (rtol 1e-2 / atol 1e-2).  The
 peer-store paths are also checked for: identical bits on every rank, identical column outputs to the NCCL path
 (same per-shard GEMV), identical row outputs of the fused and two-kernel forms, back-to-back calls alternating
-the exchange buffers, and replay of a captured CUDA graph.  Exits non-zero on any mismatch."""
+the exchange buffers, and replay of a captured CUDA graph.  Then the collective teardown (the exchange buffers'
+memory returns, released layers refuse calls) and the drop-in pair prepare_tp / kernel_fn_tp.  Exits non-zero on
+any mismatch."""
 import datetime
 import os
 import sys
@@ -38,7 +40,7 @@ def main():
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60))
     import mbp
-    from mbp.tp import TPLinear, release_tp
+    from mbp.tp import TPLinear, kernel_fn_tp, prepare_tp, release_tp
     fails = []
 
     def fail(msg):
@@ -147,6 +149,20 @@ def main():
         fail("a released layer accepted a call")
     except RuntimeError:
         pass
+
+    # 5. the drop-in pair prepare_tp / kernel_fn_tp (QKV+gate column-parallel, O row-parallel), then its release
+    st = prepare_tp({"qkv_gate": w_qkv, "o": w_o})
+    x8 = xs[0]
+    a = kernel_fn_tp({"x": x8, "config": {"m": 8, "n": 14336, "k": 6144, "layer": "qkv_gate"}}, st).clone()
+    a6 = a[:, :6144].contiguous()
+    b = kernel_fn_tp({"x": a6, "config": {"m": 8, "n": 6144, "k": 6144, "layer": "o"}}, st).clone()
+    for name, out, ref in (("qkv_gate", a, x8.float() @ w_qkv.float().T), ("o", b, a6.float() @ w_o.float().T)):
+        bad, mx = _bad(out, ref)
+        if bad:
+            fail(f"kernel_fn_tp {name}: {bad} bad, max err {mx}")
+        if not _same_on_all_ranks(out):
+            fail(f"kernel_fn_tp {name}: ranks disagree")
+    release_tp(st)
     flag = torch.tensor([1 if fails else 0], device="cuda")
     dist.all_reduce(flag)
     dist.destroy_process_group()
