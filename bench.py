@@ -1,33 +1,42 @@
-"""Benchmark of the small-M projection on B200 (the decode configuration at N=1).
+"""Benchmark of the small-M projection on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mbp|reference]
 
-Workload (one STEP): one call of each decode-GEMV shape -- fused QKV+gate (K=6144,
-N=14336) and O (K=N=6144) at M in {1, 8, 16, 32} -- with plain N(0, 0.02) weights and with the 1%-x256 escape
-variant: 16 calls.  The calls are ordered M-major over the four matrices (qkv, o, qkv-escape, o-escape), so
-between two uses of one matrix at least 250 MB of other weights stream through the 126 MB L2: every call
-reads its weights cold (inputs larger than L2; no flush kernel).  The step is captured once as a CUDA graph and
-replayed (the reference's judge also timed graph replays).
+HEADLINE STEP (config 2, the decode GEMV; identical total work at every N): one call of each decode shape --
+fused QKV+gate (K=6144, N=14336) and O (K=N=6144) at M in {1, 8, 16, 32} -- with plain N(0, 0.02) weights and
+with the 1%-x256 escape variant: 16 calls.  The calls are ordered M-major over the four matrices (qkv, o,
+qkv-escape, o-escape), so between two uses of one matrix at least 250 MB of other weights stream through the
+126 MB L2: every call reads its weights cold (inputs larger than L2).  The step is captured once as a CUDA
+graph and replayed (the reference's judge also timed graph replays).
 
-value      = packed weight bytes of a step / device time of a step (TB/s): the headline metric's bandwidth
-             form; per-shape us/call (graph replay over rotating copies of that matrix) are under "shapes".
-e2e        = the same step through the public API (mbp.kernel_fn) from pinned host buffers: H2D of x, the call
-             (new output tensor each call), D2H of the output, all inside the timed region.
-roofline   = the QKV+gate GEMV launches against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
-
---impl reference: the reference path's CPU implementation -- this build's C port of the oracle (decode +
-FP32 accumulate), all host threads -- on a bounded row sample of the same 16 calls, rank 0 only.
+value      = packed weight bytes (+ x + out) of a step / device time of a step (TB/s), max over ranks.
+e2e        = the same step through the public API (mbp.kernel_fn, or the tensor-parallel layer) from pinned
+             host buffers: H2D of x, the call (new output tensor each call), D2H of the output, all timed.
+roofline   = the 8 QKV+gate launches of the step against the measured HBM copy bandwidth (MEASURED_PEAKS.json);
+             `traffic` is read from the committed ncu summary profiles/bench_step_traffic.md.
+parity     = every output of the timed step (and of every block below) against an FP32 torch reference of the
+             same weights (rtol 1e-2 / atol 1e-2; the router: 1e-5 relative to FP64).
+Blocks of the N=1 line (per-shape us/call in CUDA-graph replays over rotating weight copies >= 400 MB):
+  shapes   config 2 per call;            verify   config 3: tcgen05 GEMM, M in {128, 256} x 4 layers, TFLOP/s
+  router   config 4: M in {1..256};      config1  M=1 4096x4096 plus the GPU pack -> unpack round trip
+  config5  the tensor-parallel shapes (M in {1, 32, 256}; qkv_gate column-, o row-parallel) unsharded, timed as
+           (L2 flush + call) - flush, like the N>1 runs;       launch_floor  fixed per-launch cost of the GEMV
+cpu_baseline / --impl reference: the reference's semantics on the host -- torch F.linear in BF16 with FP32
+accumulation (BASELINE config 1's CPU torch reference; the stand-in for candidate_sglang, submission.py
+S:2608-2615) over the FULL matrices of the same 16 calls, all host cores, the same --steps/--warmup; rank 0 only.
 Multi-GPU (torchrun, N > 1): the same step with every projection tensor-parallel over the N ranks (QKV+gate
 column-parallel + all-gather, O row-parallel + all-reduce, exchanged by the GEMV's peer stores over NVLink;
-`--transport nccl` for NCCL collectives): total work fixed ("strong" scaling), device time = max over ranks.
+`--transport nccl` for NCCL collectives): total work fixed ("strong" scaling at every N), device time = max
+over ranks, plus the config-5 block (M in {1, 32, 256}) and the parity of every output.
 --ref-shapes: kernel_fn at the reference's 30 published (M, layer) shapes against its H200 numbers (one JSON
-line, not the bench line).
+line, not the bench line).  --profile LAYER:M:VARIANT: a few calls for an ncu capture.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -42,17 +51,43 @@ METRIC = "µs/call cold-L2 & packed-weight HBM TB/s vs 8 TB/s peak, M=1–256"
 SHAPES = {"qkv_gate": (14336, 6144), "o": (6144, 6144)}
 MS = (1, 8, 16, 32)
 MATS = (("qkv_gate", "plain"), ("o", "plain"), ("qkv_gate", "esc1pct"), ("o", "esc1pct"))
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one QKV+gate M=1 launch, from one ncu capture
-NCU_TRAFFIC_QKV_M1 = 136081664
+VERIFY = {"qkv_gate": (14336, 6144), "o": (6144, 6144), "pooler": (1536, 6144), "unpooler": (6144, 1536)}
+VERIFY_MS = (128, 256)
+ROUTER_SHAPE = (256, 6144)
+ROUTER_MS = (1, 8, 16, 32, 128, 256)
+CONFIG1_SHAPE = (4096, 4096)
+TP_MS = (1, 32, 256)
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "bench_step_traffic.md")
+WORKLOAD = ("config2 decode GEMV: qkv_gate 6144->14336 and o 6144->6144, M in {1,8,16,32}, plain + 1% x256 "
+            "escape weights (16 calls per step)")
+DATA = "synthetic: W~N(0,0.02) torch seed 0 (+1% x256 variant, randperm seed 2), x~N(0,1) seed 1"
+L2_NOTE = ("inputs larger than L2: >=250 MB of other weights between reuses of a matrix in the step; per-shape "
+           "blocks rotate over weight copies >= 400 MB (config5: a 256 MB L2 flush write before every call)")
 
 
 def peaks():
+    """Roofline denominators: the driver-measured HBM copy bandwidth and cuBLAS BF16 throughput of this pool."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "kind": "measured"}
     except Exception:
-        return 6650.0, "fallback"
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "kind": "fallback"}
+
+
+def ncu_traffic():
+    """DRAM bytes per QKV+gate launch of the step (mean of its 8 launches) and where they come from: the line
+    `traffic_qkv_gate_bytes_per_launch: <int> (<source>)` of the committed ncu summary."""
+    try:
+        with open(TRAFFIC_FILE) as f:
+            for line in f:
+                mt = re.match(r"\s*traffic_qkv_gate_bytes_per_launch:\s*(\d+)\s*(.*)$", line)
+                if mt:
+                    return int(mt.group(1)), mt.group(2).strip()
+    except OSError:
+        pass
+    return None, "no committed capture"
 
 
 def make_weight(n, k, variant, device):
@@ -65,10 +100,23 @@ def make_weight(n, k, variant, device):
     return w.to(torch.bfloat16).to(device)
 
 
+def make_router_weight(device):
+    """W FP32 ~N(0, 0.01), 256 experts x 6144."""
+    import torch
+    g = torch.Generator().manual_seed(0)
+    n, k = ROUTER_SHAPE
+    return (torch.randn(n, k, generator=g) * 0.01).to(device)
+
+
 def make_x(m, k, device):
     import torch
     g = torch.Generator().manual_seed(1)
     return torch.randn(m, k, generator=g).to(torch.bfloat16).to(device)
+
+
+def call_bytes(payload: int, bases: int, m: int, n: int, k: int) -> int:
+    """Algorithmic bytes of one GEMV call: packed units + escape entries + tile bases + x + out."""
+    return payload + bases + 2 * m * k + 2 * m * n
 
 
 class Clocks:
@@ -122,53 +170,87 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_reference_run(steps: int, warmup: int, sample_rows: int):
-    """The reference path on the host: the oracle's C port (decode + FP32 accumulate) over all host threads on a
-    bounded row sample of every call.  Returns (TB/s of packed weights, seconds per sampled step, cores, text)."""
+def _bits(w):
     import numpy as np
     import torch
+    return w.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def cpu_linear_run(steps: int, warmup: int, config1: bool = True) -> dict:
+    """The reference's semantics on the host cores: torch F.linear(x, W) in BF16 with FP32 accumulation (BASELINE
+    config 1's CPU torch reference; the stand-in for candidate_sglang, submission.py S:2608-2615) over the FULL
+    matrices of the 16 calls of a step, torch.set_num_threads(all cores), `warmup` untimed and `steps` timed
+    steps.  The metric's bytes are the packed bytes the GPU arm streams for the same calls, taken from the
+    oracle's packer (the CPU reads the BF16 matrices themselves).  With `config1`, also BASELINE config 1: M=1
+    4096x4096 F.linear, and the reference format's pack -> unpack round trip of that W on the host (the oracle's
+    C restatement of sm_c12_bytes / sm_c12_unpack), which must be bit-exact."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
     from oracle import oracle
     cores = os.cpu_count() or 1
-    work, packed = [], {}
+    torch.set_num_threads(cores)
+    ws, packed_bytes = {}, {}
+    for layer, variant in MATS:
+        n, k = SHAPES[layer]
+        w = make_weight(n, k, variant, "cpu")
+        p = oracle.pack(_bits(w), tile_base=True)
+        ws[layer, variant] = w
+        packed_bytes[layer, variant] = (p["units"].nbytes + 4 * p["esc"].size, p["bases"].nbytes)
+    work, step_bytes = [], 0
     for m in MS:
         for layer, variant in MATS:
             n, k = SHAPES[layer]
-            if (layer, variant) not in packed:  # the packed sample does not depend on M
-                w = make_weight(n, k, variant, "cpu")[:sample_rows]
-                packed[layer, variant] = oracle.pack(w.view(torch.int16).numpy().view(np.uint16), tile_base=True)
-            p = packed[layer, variant]
-            x = make_x(m, k, "cpu").view(torch.int16).numpy().view(np.uint16)
-            work.append((p, x, p["units"].nbytes + p["esc"].nbytes))
+            work.append((make_x(m, k, "cpu"), ws[layer, variant]))
+            step_bytes += call_bytes(*packed_bytes[layer, variant], m, n, k)
     for _ in range(warmup):
-        for p, x, _b in work:
-            oracle.gemv_packed(x, p, threads=cores)
+        for x, w in work:
+            F.linear(x, w)
     t0 = time.perf_counter()
     for _ in range(steps):
-        for p, x, _b in work:
-            oracle.gemv_packed(x, p, threads=cores)
+        for x, w in work:
+            F.linear(x, w)
     dt = (time.perf_counter() - t0) / max(steps, 1)
-    nbytes = sum(b for _, _, b in work)
-    return nbytes / dt / 1e12, dt, cores, f"first {sample_rows} rows of each of the {len(work)} calls of a step"
+    res = {"value": step_bytes / dt / 1e12, "s_per_step": dt, "cores": cores, "step_bytes": step_bytes,
+           "sample": f"the full step: {len(work)} F.linear calls on the full BF16 matrices (qkv_gate 14336x6144, "
+                     f"o 6144x6144; plain + 1% x256), {steps} timed steps after {warmup} untimed",
+           "impl": "torch.nn.functional.linear, BF16 in/out, FP32 accumulation, CPU, "
+                   f"torch.set_num_threads({cores})"}
+    if config1:
+        n, k = CONFIG1_SHAPE
+        w = make_weight(n, k, "plain", "cpu")
+        x = make_x(1, k, "cpu")
+        F.linear(x, w)
+        ts = []
+        for _ in range(20):
+            t0 = time.perf_counter()
+            F.linear(x, w)
+            ts.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        p = oracle.pack(_bits(w), tile_base=False)  # one base per matrix: byte-identical to the reference
+        rt = oracle.unpack(p)
+        rt_s = time.perf_counter() - t0
+        res["config1"] = {"m": 1, "n": n, "k": k, "f_linear_us": round(statistics.median(ts) * 1e6, 1),
+                          "pack_roundtrip_s": round(rt_s, 3), "pack_roundtrip_exact": bool(np.array_equal(rt, _bits(w))),
+                          "n_esc": int(p["esc"].size)}
+    return res
 
 
 def run_reference(args, rank, world):
+    """--impl reference: the reference path's CPU implementation on the box's host cores (rank 0 only; the other
+    ranks of a torchrun launch exit without work)."""
     if rank != 0:
         return
-    # exactly --steps timed and --warmup untimed steps; each step is a row sample of the 16 calls (~55 ms for
-    # 1024 rows on 16 cores), shrunk so that the whole run stays near a minute
     steps, warm = max(1, args.steps), max(0, args.warmup)
-    rows = 1024
-    while rows > 16 and (steps + warm) * rows * 55e-3 / 1024 > 60.0:
-        rows //= 2
-    v, dt, cores, sample = cpu_reference_run(steps, warm, sample_rows=rows)
-    line = {"metric": METRIC, "value": round(v, 6), "unit": "TB/s", "n_gpus": args.gpus, "steps": steps,
-            "warmup": warm, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (BASELINE.json config 2 recipe)",
-            "config": {"workload": "config2 decode GEMV: qkv_gate 6144->14336 and o 6144->6144, M in {1,8,16,32}, "
-                                   "plain + 1% x256 escape weights (16 calls per step)", "l2": "n/a (host)"},
-            "impl": "reference",
-            "cpu_baseline": {"value": round(v, 6), "unit": "TB/s", "cores": cores, "kind": "port", "sample": sample},
-            "e2e": {"value": round(v, 6), "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    r = cpu_linear_run(steps, warm)
+    cb = {"value": round(r["value"], 6), "unit": "TB/s", "cores": r["cores"], "kind": "reference",
+          "sample": r["sample"], "impl": r["impl"], "config1": r.get("config1")}
+    line = {"metric": METRIC, "value": round(r["value"], 6), "unit": "TB/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": warm, "ms_per_step": round(r["s_per_step"] * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "config": {"workload": WORKLOAD, "l2": "n/a (host)", "parallelism": "host threads"},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": round(r["value"], 6), "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -184,21 +266,86 @@ def graph_of(fn, stream):
     return g
 
 
+def time_rotating(call, nrot: int, side, reps: int = 24) -> float:
+    """us per call: `reps` back-to-back calls call(i % nrot) (each reading a different weight copy, cold in L2)
+    captured in one CUDA graph; one warm replay, then two timed replays between CUDA events."""
+    import torch
+    g = graph_of(lambda: [call(i % nrot) for i in range(reps)], side)
+    g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (2 * reps)
+
+
+def time_after_flush(call, flush, inner: int = 10, reps: int = 10) -> float:
+    """us per call measured as (L2 flush write + call) - (flush write alone): graphs of `inner` pairs, replayed
+    `reps` times between CUDA events; every call starts with a cold L2 (256 MB written before it)."""
+    import torch
+
+    def timed(fn):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(inner):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        del g
+        return a.elapsed_time(b) * 1e3 / (reps * inner)
+
+    def pair():
+        flush.fill_(1)
+        call()
+
+    return timed(pair) - timed(lambda: flush.fill_(1))
+
+
+def c12_copies(p, min_bytes: int = 400 << 20):
+    """The packed matrix plus clones of its units (same bases and escapes) totalling >= min_bytes."""
+    import mbp
+    nc = max(3, -(-min_bytes // p.units.numel()))
+    return [p] + [mbp.PackedC12(p.units.clone(), p.bases, p.esc_off, p.esc, p.n, p.k, p.n_esc) for _ in range(nc - 1)]
+
+
+def close_check(out, ref, rtol=1e-2, atol=1e-2) -> tuple[bool, float]:
+    err = (out.float() - ref).abs()
+    ok = bool((err <= atol + rtol * ref.abs()).all()) and bool(out.float().isfinite().all())
+    return ok, float(err.max())
+
+
 def run_mbp(args, rank, world):
     import torch
-    import torch.distributed as dist
     import mbp
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
     torch.cuda.set_device(dev)
     side = torch.cuda.Stream()
+    pk = peaks()
 
-    states, packed = {}, {}
+    states, packed, weights = {}, {}, {}
     for layer, variant in MATS:
         n, k = SHAPES[layer]
-        st = mbp.prepare({layer: make_weight(n, k, variant, dev)})
+        w = make_weight(n, k, variant, dev)
+        st = mbp.prepare({layer: w})
         states[(layer, variant)] = st
         packed[(layer, variant)] = st["layers"][layer]
+        weights[(layer, variant)] = w
     torch.cuda.empty_cache()
     calls = []  # name, layer, variant, m, packed, x_dev, out_dev, x_host, out_host, bytes
     for m in MS:
@@ -209,7 +356,7 @@ def run_mbp(args, rank, world):
             out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
             xh = x.cpu().pin_memory()
             oh = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
-            nbytes = p.payload_bytes + p.bases.numel() + 2 * m * k + 2 * m * n
+            nbytes = call_bytes(p.payload_bytes, p.bases.numel(), m, n, k)
             calls.append((f"{layer}_m{m}_{variant}", layer, variant, m, p, x, out, xh, oh, nbytes))
     step_bytes = sum(c[-1] for c in calls)
 
@@ -227,48 +374,143 @@ def run_mbp(args, rank, world):
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     with Clocks(dev.index) as clk:
-        if world > 1:
-            dist.barrier()
         torch.cuda.synchronize()
         a.record()
         for _ in range(args.steps):
             g_step.replay()
         b.record()
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
     clocks = clk.summary()
     step_ms = a.elapsed_time(b) / args.steps
     assert mbp.device_status() == 0, "device status word set during the timed region"
-    if world > 1:
-        t = torch.tensor([step_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        step_ms = float(t.item())
-    value = step_bytes * world / (step_ms * 1e-3) / 1e12
+    value = step_bytes / (step_ms * 1e-3) / 1e12
 
-    # ---------------- per-shape us/call: graph over rotating copies of one matrix ----------------
+    # ---------------- parity of the timed step's outputs ----------------
+    par_ok, par_err = True, 0.0
+    for c in calls:
+        ok, err = close_check(c[6], c[5].float() @ weights[(c[1], c[2])].float().T)
+        par_ok &= ok
+        par_err = max(par_err, err)
+    parity = {"status": "ok" if par_ok else "FAIL", "calls_checked": len(calls), "max_abs_err": round(par_err, 5),
+              "rule": "every output of the timed step within rtol 1e-2 / atol 1e-2 of x.float() @ W.float().T"}
+
+    # ---------------- config 2 per shape: graph over rotating copies of one matrix ----------------
     shapes = {}
-    reps = 24
     for (layer, variant), p0 in packed.items():
-        nc = max(3, (400 << 20) // p0.units.numel())
-        ps = [p0] + [mbp.PackedC12(p0.units.clone(), p0.bases, p0.esc_off, p0.esc, p0.n, p0.k, p0.n_esc)
-                     for _ in range(nc - 1)]
+        ps = c12_copies(p0)
         for c in calls:
             if (c[1], c[2]) != (layer, variant):
                 continue
-            g = graph_of(lambda: [mbp.gemv(ps[i % nc], c[5], out=c[6]) for i in range(reps)], side)
-            g.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            g.replay()
-            g.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / (2 * reps)
-            shapes[c[0]] = {"us": round(us, 2), "tbps": round(c[-1] / us / 1e6, 3), "bytes": c[-1]}
-            del g
+            us = time_rotating(lambda i, c=c: mbp.gemv(ps[i], c[5], out=c[6]), len(ps), side)
+            shapes[c[0]] = {"us": round(us, 2), "tbps": round(c[-1] / us / 1e6, 3), "bytes": c[-1],
+                            "frac_hbm": round(c[-1] / us / 1e3 / pk["hbm_gbs"], 4)}
         del ps
         torch.cuda.empty_cache()
+
+    # ---------------- fixed per-launch cost of the GEMV (M = 1, qkv_gate plain) ----------------
+    # the full matrix and its first half (n_out = 7168, the column-parallel shard geometry): the difference
+    # gives the steady streaming rate, the remainder of the full call the fill + drain of one launch
+    p0 = packed[("qkv_gate", "plain")]
+    ps = c12_copies(p0)
+    x1 = make_x(1, p0.k, dev)
+    oh = torch.empty((1, p0.n), dtype=torch.bfloat16, device=dev)
+    us_full = time_rotating(lambda i: mbp.gemv(ps[i], x1, out=oh), len(ps), side, reps=48)
+    us_half = time_rotating(lambda i: mbp.gemv(ps[i], x1, n_out=p0.n // 2, out=oh), len(ps), side, reps=48)
+    del ps
+    b_full = call_bytes(p0.payload_bytes, p0.bases.numel(), 1, p0.n, p0.k)
+    b_half = call_bytes(p0.payload_bytes // 2, p0.bases.numel() // 2, 1, p0.n // 2, p0.k)
+    rate = (b_full - b_half) / max(us_full - us_half, 1e-3) / 1e6
+    launch_floor = {"qkv_gate_m1_us": round(us_full, 2), "half_rows_m1_us": round(us_half, 2),
+                    "steady_tbps": round(rate, 3), "floor_us": round(us_full - b_full / rate / 1e6, 2),
+                    "how": "floor = us(full) - bytes(full) / steady rate; steady rate = delta bytes / delta us "
+                           "between the full matrix and its first half (n_out = 7168)"}
+
+    # ---------------- config 3: the tcgen05 verify GEMM ----------------
+    verify = {}
+    for layer, (n, k) in VERIFY.items():
+        w = make_weight(n, k, "plain", dev)
+        st = mbp.prepare({layer: w})
+        ps = c12_copies(st["layers"][layer])
+        for m in VERIFY_MS:
+            x = make_x(m, k, dev)
+            out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+            us = time_rotating(lambda i: mbp.gemm(ps[i], x, out=out), len(ps), side, reps=16)
+            o = mbp.kernel_fn({"x": x, "config": {"m": m, "n": n, "k": k, "layer": layer}}, st)
+            ok, err = close_check(o, x.float() @ w.float().T)
+            tf = 2.0 * m * n * k / (us * 1e-6) / 1e12
+            nbytes = call_bytes(ps[0].payload_bytes, ps[0].bases.numel(), m, n, k)
+            verify[f"{layer}_m{m}"] = {
+                "us": round(us, 2), "tflops": round(tf, 1), "frac_tensor": round(tf / pk["bf16_tflops"], 4),
+                "frac_tensor_sustained": round(tf / pk["bf16_tflops_sustained"], 4),
+                "tbps": round(nbytes / us / 1e6, 3), "frac_hbm": round(nbytes / us / 1e3 / pk["hbm_gbs"], 4),
+                "parity": "ok" if ok else "FAIL", "max_abs_err": round(err, 5)}
+            par_ok &= ok
+        del ps, st
+        torch.cuda.empty_cache()
+
+    # ---------------- config 4: the FP32 router through the BF16 hi/lo pair ----------------
+    router = {}
+    wr = make_router_weight(dev)
+    st_r = mbp.prepare({"router": wr})
+    pr = st_r["hilo"]["router"]
+    nrot = max(3, -(-(256 << 20) // pr.units.numel()))
+    prs = [pr] + [mbp.PackedHiLo(pr.units.clone(), pr.n, pr.k) for _ in range(nrot - 1)]
+    for m in ROUTER_MS:
+        x = make_x(m, pr.k, dev)
+        out = torch.empty((m, pr.n), dtype=torch.float32, device=dev)
+        us = time_rotating(lambda i: mbp.router(prs[i], x, out=out), nrot, side, reps=32)
+        o = mbp.kernel_fn({"x": x, "config": {"m": m, "n": pr.n, "k": pr.k, "layer": "router"}}, st_r)
+        ref = x.double() @ wr.double().T
+        rel = float((o.double() - ref).norm() / ref.norm())
+        nbytes = pr.payload_bytes + 2 * m * pr.k + 4 * m * pr.n
+        router[f"m{m}"] = {"us": round(us, 2), "tbps": round(nbytes / us / 1e6, 3),
+                           "frac_hbm": round(nbytes / us / 1e3 / pk["hbm_gbs"], 4),
+                           "rel_err_vs_fp64": float(f"{rel:.3g}"), "parity": "ok" if rel <= 1e-5 else "FAIL"}
+        par_ok &= rel <= 1e-5
+    del prs, st_r
+    torch.cuda.empty_cache()
+
+    # ---------------- config 1 on the GPU: M=1 4096x4096 and the pack round trip ----------------
+    n, k = CONFIG1_SHAPE
+    w1 = make_weight(n, k, "plain", dev)
+    mbp.pack_c12(w1, mbp.BASE_MATRIX)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    p1 = mbp.pack_c12(w1, mbp.BASE_MATRIX)  # one base per matrix: byte-identical to the reference's packer
+    rt = mbp.unpack_c12(p1)
+    torch.cuda.synchronize()
+    rt_ms = (time.perf_counter() - t0) * 1e3
+    exact = bool(torch.equal(rt, w1))
+    ps = c12_copies(p1)
+    x = make_x(1, k, dev)
+    out = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+    us = time_rotating(lambda i: mbp.gemv(ps[i], x, out=out), len(ps), side, reps=48)
+    ok, err = close_check(mbp.gemv(p1, x), x.float() @ w1.float().T)
+    nbytes = call_bytes(p1.payload_bytes, p1.bases.numel(), 1, n, k)
+    config1 = {"m": 1, "n": n, "k": k, "us": round(us, 2), "tbps": round(nbytes / us / 1e6, 3),
+               "pack_roundtrip_ms": round(rt_ms, 2), "pack_roundtrip_exact": exact, "n_esc": p1.n_esc,
+               "parity": "ok" if ok else "FAIL", "max_abs_err": round(err, 5)}
+    par_ok &= ok and exact
+    del ps, p1, rt
+    torch.cuda.empty_cache()
+
+    # ---------------- config 5 shapes, unsharded (the N>1 runs time the same calls tensor-parallel) --------
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    config5 = {}
+    for layer in ("qkv_gate", "o"):
+        p, w = packed[(layer, "plain")], weights[(layer, "plain")]
+        for m in TP_MS:
+            x = make_x(m, p.k, dev)
+            fn = (lambda: mbp.gemv(p, x)) if m <= mbp.GEMV_MAX_M else (lambda: mbp.gemm(p, x))
+            us = time_after_flush(fn, flush)
+            ok, err = close_check(fn(), x.float() @ w.float().T)
+            config5[f"{layer}_m{m}"] = {"us": round(us, 2), "parity": "ok" if ok else "FAIL"}
+            par_ok &= ok
+    del flush
+    torch.cuda.empty_cache()
+    parity["status"] = "ok" if par_ok else "FAIL"
+    parity["blocks"] = "the step, shapes of config1/3/4/5 (router: 1e-5 relative to FP64; config1: bit-exact pack)"
+    assert mbp.device_status() == 0
 
     # ---------------- e2e through the public API with host buffers ----------------
     # Each call: its x travels host -> device on a copy stream, kernel_fn runs on the compute stream as soon as
@@ -307,9 +549,8 @@ def run_mbp(args, rank, world):
     e1.record()
     torch.cuda.synchronize()
     eager_ms = e0.elapsed_time(e1) / e2e_steps
-    # headline e2e: the same public-API step (pinned-host -> device copy of x, kernel_fn, device -> pinned-host
-    # copy of the output, per call) captured once in a CUDA graph and replayed, as the reference's harness replays
-    # kernel_fn
+    # headline e2e: the same public-API step captured once in a CUDA graph and replayed, as the reference's
+    # harness replays kernel_fn
     g_api = graph_of(api_step, side)
     for _ in range(3):
         g_api.replay()
@@ -321,44 +562,52 @@ def run_mbp(args, rank, world):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     del g_api
+    e2e_ok = all(torch.equal(c[8], c[6].cpu()) for c in calls)  # the host copies hold the step's outputs
     h2d = sum(2 * c[3] * c[4].k for c in calls)
     d2h = sum(2 * c[3] * c[4].n for c in calls)
 
-    hbm, peak_kind = peaks()
     dom = [c[0] for c in calls if c[1] == "qkv_gate"]
     dom_bytes = sum(shapes[nm]["bytes"] for nm in dom)
     dom_us = sum(shapes[nm]["us"] for nm in dom)
     achieved = dom_bytes / (dom_us * 1e-6) / 1e9
+    traffic, traffic_src = ncu_traffic()
 
     if rank == 0:
         cpu = None
-        if world == 1 and not args.no_cpu:
-            v, dt, cores, sample = cpu_reference_run(1, 0, sample_rows=512)
-            cpu = {"value": round(v, 6), "unit": "TB/s", "cores": cores, "kind": "port", "sample": sample}
+        if not args.no_cpu:
+            r = cpu_linear_run(args.steps, args.warmup)
+            cpu = {"value": round(r["value"], 6), "unit": "TB/s", "cores": r["cores"], "kind": "reference",
+                   "sample": r["sample"], "impl": r["impl"], "ms_per_step": round(r["s_per_step"] * 1e3, 3),
+                   "config1": r.get("config1")}
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: W~N(0,0.02) torch seed 0 (+1% x256 variant, randperm seed 2), x~N(0,1) seed 1",
-            "config": {"workload": "config2 decode GEMV: qkv_gate 6144->14336 and o 6144->6144, M in {1,8,16,32}, "
-                                   "plain + 1% x256 escape weights (16 calls per step)",
-                       "l2": "cold by construction: >=250 MB of other weights between reuses of a matrix "
-                             "(inputs larger than L2), no flush kernel",
+            "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "config": {"workload": WORKLOAD, "l2": L2_NOTE,
                        "timing": "CUDA-graph replay of the step, CUDA events on the replay stream",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "traffic": NCU_TRAFFIC_QKV_M1,
-                         "kernel": "k_gemv, the 8 qkv_gate launches of a step", "peak_kind": f"{peak_kind} hbm_gbs",
-                         "frac_of_8tbps": round(achieved / 8000.0, 4)},
+                       "parallelism": "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+                         "traffic_source": traffic_src,
+                         "algorithmic_bytes_per_launch": int(dom_bytes / len(dom)),
+                         "kernel": "the 8 qkv_gate launches of a step (weight-streaming GEMV)",
+                         "peak_kind": f"{pk['kind']} hbm_gbs", "frac_of_8tbps": round(achieved / 8000.0, 4)},
             "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                     "timing": "CUDA-graph replay of the public-API step (per call: H2D of x on a copy stream, "
                               "kernel_fn, D2H of out on a second copy stream, overlapping the other calls)",
-                    "eager_ms_per_step": round(eager_ms, 4)},
+                    "eager_ms_per_step": round(eager_ms, 4), "outputs_match_device": e2e_ok},
             "gpu_launches": len(calls) * args.steps,
             "clocks": clocks,
+            "parity": parity,
             "cpu_baseline": cpu,
             "shapes": shapes,
+            "verify": verify,
+            "router": router,
+            "config1": config1,
+            "config5": config5,
+            "launch_floor": launch_floor,
+            "peaks": pk,
         }
         print(json.dumps(line), flush=True)
 
@@ -366,8 +615,10 @@ def run_mbp(args, rank, world):
 def run_mbp_tp(args, rank, world):
     """N > 1: the same 16-call step, each projection tensor-parallel over the N ranks (QKV+gate column-parallel
     + all-gather, O row-parallel + all-reduce of FP32 partials; by default through the GEMV's peer stores with
-    the receive fused into it, `--transport nccl` for NCCL collectives).  Total work is fixed
-    (strong scaling); value = packed bytes of the unsharded layers per step / step time (max over ranks)."""
+    the receive fused into it, `--transport nccl` for NCCL collectives).  Total work is fixed (strong scaling);
+    value = bytes of the unsharded calls per step / step time (max over ranks).  After timing, every output of
+    the step and of the config-5 calls (M in {1, 32, 256}, through the GEMM + NCCL at M = 256) is compared with
+    the FP32 reference of the full weights and with the unsharded single-GPU kernels."""
     import torch
     import torch.distributed as dist
     import mbp
@@ -375,28 +626,30 @@ def run_mbp_tp(args, rank, world):
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
     torch.cuda.set_device(dev)
-    lins = {}
+    pk = peaks()
+    lins, weights, full = {}, {}, {}
     for layer, variant in MATS:
         n, k = SHAPES[layer]
-        lins[(layer, variant)] = TPLinear(make_weight(n, k, variant, dev), "column" if layer == "qkv_gate" else "row",
-                                          transport=args.transport)
+        w = make_weight(n, k, variant, dev)
+        weights[(layer, variant)] = w
+        full[(layer, variant)] = mbp.pack_c12(w)  # unsharded packing: the parity check's single-GPU result
+        lins[(layer, variant)] = TPLinear(w, "column" if layer == "qkv_gate" else "row", transport=args.transport)
     transport = next(iter(lins.values())).transport
     torch.cuda.empty_cache()
-    shard_bytes = {key: torch.tensor([lin.payload_bytes], device=dev) for key, lin in lins.items()}
-    for t in shard_bytes.values():
-        dist.all_reduce(t)
-    calls = []
+    calls = []  # name, layer, m, x, bytes (of the unsharded call), key
     for m in MS:
         for layer, variant in MATS:
             n, k = SHAPES[layer]
-            x = make_x(m, k, dev)
-            nbytes = int(shard_bytes[(layer, variant)].item()) + 2 * m * k + 2 * m * n
-            calls.append((f"{layer}_m{m}_{variant}", lins[(layer, variant)], x, nbytes, m, n, k))
+            p = full[(layer, variant)]
+            calls.append((f"{layer}_m{m}_{variant}", lins[(layer, variant)], make_x(m, k, dev),
+                          call_bytes(p.payload_bytes, p.bases.numel(), m, n, k), m, n, k, (layer, variant)))
     step_bytes = sum(c[3] for c in calls)
+    outs: list = []
 
     def step():
+        outs.clear()
         for c in calls:
-            c[1](c[2])
+            outs.append(c[1](c[2]))
 
     for _ in range(args.warmup):
         step()
@@ -418,6 +671,10 @@ def run_mbp_tp(args, rank, world):
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     use_graph = int(ok.item()) == 1
     run = (lambda: g.replay()) if use_graph else step
+    if not use_graph and g is not None:
+        del g
+        g = None
+        step()
     for _ in range(3):
         run()
     torch.cuda.synchronize()
@@ -437,7 +694,51 @@ def run_mbp_tp(args, rank, world):
     t = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     step_ms = float(t.item())
-    assert mbp.device_status() == 0
+    status_ok = mbp.device_status() == 0
+
+    # parity of the timed step: outs hold the last replay's outputs
+    par_ok, par_err, diff_unsharded = status_ok, 0.0, 0.0
+    for c, o in zip(calls, outs):
+        w = weights[c[7]]
+        ok1, err = close_check(o, c[2].float() @ w.float().T)
+        par_ok &= ok1
+        par_err = max(par_err, err)
+        diff_unsharded = max(diff_unsharded, float((o.float() - mbp.gemv(full[c[7]], c[2]).float()).abs().max()))
+
+    # config 5: M in {1, 32, 256} (qkv_gate column-parallel, o row-parallel; plain weights), each call timed as
+    # (L2 flush write + call) - flush alone, max over ranks; outputs checked like the step's
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    config5 = {}
+    for layer in ("qkv_gate", "o"):
+        lin, w, p = lins[(layer, "plain")], weights[(layer, "plain")], full[(layer, "plain")]
+        for m in TP_MS:
+            x = make_x(m, p.k, dev)
+            us = torch.tensor([time_after_flush(lambda: lin(x), flush)], device=dev)
+            dist.all_reduce(us, op=dist.ReduceOp.MAX)
+            o = lin(x)
+            ok1, err = close_check(o, x.float() @ w.float().T)
+            single = mbp.gemv(p, x) if m <= mbp.GEMV_MAX_M else mbp.gemm(p, x)
+            diff_unsharded = max(diff_unsharded, float((o.float() - single.float()).abs().max()))
+            par_ok &= ok1
+            par_err = max(par_err, err)
+            config5[f"{layer}_m{m}"] = {"us": round(float(us.item()), 2), "parity": "ok" if ok1 else "FAIL",
+                                        "path": ("GEMV + " + ("peer-store exchange" if transport == "p2p"
+                                                              else "NCCL")) if m <= mbp.GEMV_MAX_M
+                                        else "tcgen05 GEMM + NCCL " + ("all-gather" if layer == "qkv_gate"
+                                                                       else "all-reduce")}
+    del flush
+    torch.cuda.synchronize()
+    status_ok &= mbp.device_status() == 0
+    par_ok &= status_ok
+    flag = torch.tensor([1 if par_ok else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    errs = torch.tensor([par_err, diff_unsharded], device=dev)
+    dist.all_reduce(errs, op=dist.ReduceOp.MAX)
+    parity = {"status": "ok" if int(flag.item()) == 1 else "FAIL", "calls_checked": len(calls) + 2 * len(TP_MS),
+              "ranks": world, "max_abs_err_vs_fp32": round(float(errs[0]), 5),
+              "max_abs_diff_vs_unsharded": round(float(errs[1]), 5), "device_status_clear": status_ok,
+              "rule": "every rank's output of every call within rtol 1e-2 / atol 1e-2 of x.float() @ W.float().T "
+                      "(full weights); the difference to the unsharded single-GPU kernels is reported"}
 
     # e2e: host x in, host output back, every call, through the layers' public forward: as at N = 1, each call's
     # x travels host -> device on a copy stream and its output device -> host on a second one, overlapping the
@@ -491,27 +792,27 @@ def run_mbp_tp(args, rank, world):
         for _ in range(3):
             g_api.replay()
     e2e_ms = timed_max(g_api.replay, e2e_steps) if g_api is not None else eager_e2e_ms
-    hbm, peak_kind = peaks()
+    # our kernels per call of the step: one (the fused peer-store GEMV), or the GEMV plus the receive kernel /
+    # the assembly or BF16-rounding kernel after NCCL
+    per_call = [1 if (transport == "p2p" and c[1].fused and c[4] not in c[1]._two_kernel_m) else 2 for c in calls]
     if rank == 0:
         value = step_bytes / (step_ms * 1e-3) / 1e12
         line = {
             "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: W~N(0,0.02) torch seed 0 (+1% x256 variant, randperm seed 2), x~N(0,1) seed 1",
-            "config": {"workload": "config2 decode GEMV step (16 calls), tensor-parallel: qkv_gate column-parallel + "
-                                   "all-gather, o row-parallel + all-reduce of FP32 partials",
+            "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "config": {"workload": WORKLOAD + ", tensor-parallel: qkv_gate column-parallel + all-gather, o "
+                                              "row-parallel + all-reduce of FP32 partials",
                        "transport": ("one kernel per call: the shard GEMV stores epoch-tagged words into every "
                                      "rank's buffer over NVLink (CUDA IPC) and its CTAs assemble their tiles"
                                      if transport == "p2p" else "NCCL collectives"),
-                       "l2": "cold by construction (>=250 MB of other weights between reuses of a matrix on one GPU "
-                             "at N=1; per-GPU shards at N>1)",
+                       "l2": L2_NOTE,
                        "timing": ("CUDA-graph replay" if use_graph else "eager launches") +
                                  " of the step, CUDA events, max over ranks",
                        "parallelism": f"tp{world}"},
-            "roofline": {"bound": "hbm", "achieved": round(value * 1e3 / world, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(value * 1e3 / world / hbm, 4), "traffic": None,
-                         "kernel": "whole step per GPU (GEMV + collectives)", "peak_kind": f"{peak_kind} hbm_gbs"},
+            "roofline": {"bound": "hbm", "achieved": round(value * 1e3 / world, 1), "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(value * 1e3 / world / pk["hbm_gbs"], 4), "traffic": None,
+                         "kernel": "whole step per GPU (shard GEMVs + exchange)", "peak_kind": f"{pk['kind']} hbm_gbs"},
             "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
                     "h2d_bytes_per_step": sum(2 * c[4] * c[6] for c in calls),
                     "d2h_bytes_per_step": sum(2 * c[4] * c[5] for c in calls), "ms_per_step": round(e2e_ms, 4),
@@ -519,9 +820,10 @@ def run_mbp_tp(args, rank, world):
                               " of the public-API step (per call: H2D of x on a copy stream, the layer's forward, "
                               "D2H of out on a second copy stream, overlapping the other calls), max over ranks",
                     "eager_ms_per_step": round(eager_e2e_ms, 4)},
-            # per call: the GEMV + the finish kernel (p2p) or the assemble / BF16-rounding kernel after NCCL
-            "gpu_launches": 2 * len(calls) * args.steps,
+            "gpu_launches": sum(per_call) * args.steps,
             "clocks": clocks,
+            "parity": parity,
+            "config5": config5,
             "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)
@@ -530,6 +832,9 @@ def run_mbp_tp(args, rank, world):
     if g_api is not None:
         del g_api
     torch.cuda.synchronize()
+    dist.barrier()
+    for lin in lins.values():  # collective teardown of the exchange buffers, the same order on every rank
+        lin.close()
 
 
 # The reference's published per-shape times (us, NVIDIA H200, v18 submission, results/v18_shapes.csv:2-31) at its
@@ -666,27 +971,48 @@ def run_ref_shapes(reps: int = 200):
 
 
 def run_profile(spec: str, launches: int = 3):
-    """--profile LAYER:M:VARIANT -- a few launches of one call for an ncu capture (no timing, no output)."""
+    """--profile LAYER:M:VARIANT -- a few calls of one shape for an ncu capture (no timing, no output).  LAYER is
+    qkv_gate / o (config 2 shapes, VARIANT plain or esc1pct), pooler / unpooler (config 3), or router; `step`
+    instead runs one warm-up and one timed-region-like pass of the 16-call headline step."""
     import torch
     import mbp
-    layer, m, variant = spec.split(":")
-    n, k = SHAPES[layer]
     torch.cuda.set_device(0)
-    st = mbp.prepare({layer: make_weight(n, k, variant, "cuda")})
-    x = make_x(int(m), k, "cuda")
+    if spec == "step":
+        ps = {}
+        for layer, variant in MATS:
+            n, k = SHAPES[layer]
+            ps[layer, variant] = mbp.prepare({layer: make_weight(n, k, variant, "cuda")})["layers"][layer]
+        xs = {m: {layer: make_x(m, SHAPES[layer][1], "cuda") for layer in SHAPES} for m in MS}
+        for _ in range(2):
+            for m in MS:
+                for layer, variant in MATS:
+                    mbp.gemv(ps[layer, variant], xs[m][layer])
+        torch.cuda.synchronize()
+        assert mbp.device_status() == 0
+        print("profile run ok: step")
+        return
+    layer, m, variant = spec.split(":")
+    m = int(m)
+    if layer == "router":
+        w = make_router_weight("cuda")
+        n, k = w.shape
+    else:
+        n, k = SHAPES.get(layer) or VERIFY[layer]
+        w = make_weight(n, k, variant, "cuda")
+    st = mbp.prepare({layer: w})
+    x = make_x(m, k, "cuda")
     for _ in range(launches):
-        mbp.kernel_fn({"x": x, "config": {"m": int(m), "n": n, "k": k, "layer": layer}}, st)
+        mbp.kernel_fn({"x": x, "config": {"m": m, "n": n, "k": k, "layer": layer}}, st)
     torch.cuda.synchronize()
     assert mbp.device_status() == 0
-    path = st["layers"][layer].plan(int(m)).as_tuple() if int(m) <= mbp.GEMV_MAX_M else "tcgen05 gemm"
-    print("profile run ok:", spec, path)
+    print("profile run ok:", spec)
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--profile", default=None, help="LAYER:M:VARIANT: a few launches of one call, for ncu")
+    ap.add_argument("--profile", default=None, help="LAYER:M:VARIANT (or `step`): a few launches, for ncu")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mbp", choices=["mbp", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
@@ -704,19 +1030,18 @@ def main():
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        # host-only arm: no process group (the other ranks of a torchrun launch exit at once)
+        run_reference(args, rank, world)
+        return
     if world > 1:
         import datetime
         import torch
         import torch.distributed as dist
-        if args.impl == "mbp":
-            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-        else:
-            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     try:
-        if args.impl == "reference":
-            run_reference(args, rank, world)
-        elif world > 1:
+        if world > 1:
             run_mbp_tp(args, rank, world)
         else:
             run_mbp(args, rank, world)

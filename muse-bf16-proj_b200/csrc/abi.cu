@@ -1,5 +1,15 @@
-// Library-level entry points: version, device check, and the device status word (one per translation unit).
+// Library-level entry points: version, device check, the device status word (one per translation unit) and the
+// limit of the kernels' bounded waits.
+#include <atomic>
+
 #include "common.cuh"
+
+namespace mbp {
+namespace {
+std::atomic<unsigned long long> g_wait_ns{kDefaultWaitLimitNs};
+}
+uint64_t wait_limit_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
+}  // namespace mbp
 
 int mbp_status_pack(int* v, int clear);
 int mbp_status_gemv(int* v, int clear);
@@ -17,6 +27,10 @@ int mbp_device_check(int device) {
     return MBP_ERR_DEVICE;
   }
   return prop.major == 10 && prop.minor == 0 ? MBP_OK : MBP_ERR_DEVICE;
+}
+
+unsigned long long mbp_set_wait_limit(unsigned long long ns) {
+  return mbp::g_wait_ns.exchange(ns ? ns : mbp::kDefaultWaitLimitNs);
 }
 
 int mbp_status(int* status, int clear) {

@@ -40,7 +40,11 @@ MBP_DEV uint64_t globaltimer() {
   return t;
 }
 
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s: a wait this long means a lost arrival
+// Limit of every bounded wait.  Each launch copies the library-wide setting (mbp_set_wait_limit, default 1 s: a
+// wait this long means a lost arrival) into its parameters, so a kernel captured in a CUDA graph keeps the limit
+// in force when it was captured.
+constexpr uint64_t kDefaultWaitLimitNs = 1000000000ull;
+uint64_t wait_limit_ns();  // host: the current setting (abi.cu)
 
 // Single-copy-atomic 64-bit accesses at system scope (epoch-tagged words exchanged between GPUs).
 MBP_DEV void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
@@ -53,15 +57,15 @@ MBP_DEV uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
 }
 
 // Bounded wait for an exchange word tagged with epoch e (tag in the upper 32 bits; data and tag arrive in one
-// store).  t0 = 0 on the first call of a thread; after kWaitLimitNs the status word gets MBP_DEV_TIMEOUT_PEER
-// and `dead` stops further waits of the thread (the words are then read as they are).
-MBP_DEV uint64_t wait_tag(const uint64_t* p, uint32_t e, uint64_t& t0, bool& dead) {
+// store).  t0 = 0 on the first call of a thread; once `limit` ns have passed since then the status word gets
+// MBP_DEV_TIMEOUT_PEER and `dead` stops further waits of the thread (the words are then read as they are).
+MBP_DEV uint64_t wait_tag(const uint64_t* p, uint32_t e, uint64_t& t0, bool& dead, uint64_t limit) {
   uint64_t v = ld_relaxed_sys_u64(p);
   while ((uint32_t)(v >> 32) != e && !dead) {
     const uint64_t now = globaltimer();
     if (t0 == 0) {
       t0 = now;
-    } else if (now - t0 > kWaitLimitNs) {
+    } else if (now - t0 > limit) {
       set_status(MBP_DEV_TIMEOUT_PEER);
       dead = true;
     }
@@ -123,12 +127,12 @@ MBP_DEV bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
   return ok != 0;
 }
 
-// Bounded wait: returns false (and records `code`) if the phase did not complete within kWaitLimitNs.
-MBP_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int code) {
+// Bounded wait: returns false (and records `code`) if the phase did not complete within `limit` ns.
+MBP_DEV bool mbar_wait(uint32_t bar, uint32_t parity, int code, uint64_t limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit) {
       set_status(code);
       return false;
     }

@@ -73,6 +73,7 @@ struct __align__(64) GemvParams {
   int rb, split, wki, kci, stages;
   int nblk;     // row blocks: block b owns row tiles [b*Rout/nblk, (b+1)*Rout/nblk), at most rb of them
   int has_esc;  // the matrix has escapes: consumer warps get escape masks
+  unsigned long long wait_ns;  // limit of every bounded wait
 };
 
 // Chunks per unrolled consumer pass and independent accumulators per (row tile, token tile), sized so that a
@@ -193,7 +194,7 @@ MBP_DEV void tp_receive(const GemvParams& p, uint32_t epoch, int r0, int rvalid,
       const uint64_t* w = words + (size_t)t * half + q * (ns / 2) + (r0 + rr) * 8;
       uint32_t d[8];
 #pragma unroll
-      for (int g = 0; g < 8; ++g) d[g] = (uint32_t)wait_tag(w + g, epoch, t0, dead);
+      for (int g = 0; g < 8; ++g) d[g] = (uint32_t)wait_tag(w + g, epoch, t0, dead, p.wait_ns);
       uint4 lo, hi;
       lo.x = (d[0] & 0xffffu) | d[1] << 16;
       lo.y = (d[2] & 0xffffu) | d[3] << 16;
@@ -216,7 +217,7 @@ MBP_DEV void tp_receive(const GemvParams& p, uint32_t epoch, int r0, int rvalid,
         const uint64_t* w = words + ((size_t)q * p.m + t) * p.rn + row;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float f = __uint_as_float((uint32_t)wait_tag(w + j, epoch, t0, dead));
+          const float f = __uint_as_float((uint32_t)wait_tag(w + j, epoch, t0, dead, p.wait_ns));
           a[j] = q == 0 ? f : a[j] + f;
         }
       }
@@ -315,7 +316,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
     for (int it = 0; it < nit; ++it) {
       const int st = it % p.stages;
       const uint32_t ph = (uint32_t)(it / p.stages) & 1u;
-      if (it >= p.stages && !mbar_wait(empty0 + 8 * st, ph ^ 1u, MBP_DEV_TIMEOUT_EMPTY)) break;
+      if (it >= p.stages && !mbar_wait(empty0 + 8 * st, ph ^ 1u, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
       uint32_t bytes = 0;
       for (int q = 0; q < p.wki; ++q) {
         const int c0 = cs + q * Lk + it * p.kci, e = min(cs + (q + 1) * Lk, ce);
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
     for (int it = 0; it < nit; ++it) {
       const int st = it % p.stages;
       const uint32_t ph = (uint32_t)(it / p.stages) & 1u;
-      if (!mbar_wait(full0 + 8 * st, ph, MBP_DEV_TIMEOUT_FULL)) break;
+      if (!mbar_wait(full0 + 8 * st, ph, MBP_DEV_TIMEOUT_FULL, p.wait_ns)) break;
       const unsigned char* stage = smem + st * L.sbytes;
       const int c0 = b + it * p.kci;
       const int nk = rvalid_j[0] ? max(0, min(p.kci, e - c0)) : 0;  // a warp without valid rows only drains
@@ -986,6 +987,7 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   p.stages = g.stages;
   p.nblk = nblk;
   p.has_esc = with_esc ? 1 : 0;
+  p.wait_ns = wait_limit_ns();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nblk, g.split, (m + tok - 1) / tok);
   cfg.blockDim = dim3(32 * (rows_w * g.wki + 1));

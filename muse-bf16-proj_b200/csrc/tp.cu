@@ -62,6 +62,7 @@ struct TPFinish {
   void* out;
   int m, n;               // output [m][n]
   int rank, P, mode;
+  unsigned long long wait_ns;  // limit of every bounded wait
 };
 
 MBP_DEV int ld_acquire_sys(const int* p) {
@@ -88,7 +89,7 @@ __global__ void __launch_bounds__(kSlots) k_tp_barrier(const __grid_constant__ T
     const int* mine = s.flags[s.rank] + l;
     const uint64_t t0 = globaltimer();
     while (ld_acquire_sys(mine) < e) {
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > s.wait_ns) {
         set_status(MBP_DEV_TIMEOUT_PEER);
         break;
       }
@@ -124,7 +125,7 @@ __global__ void __launch_bounds__(kRecvThreads) k_tp_recv(const __grid_constant_
       const uint64_t* w = words + (long long)t * (s.n / 2) + tile * 8;
       uint32_t d[8];
 #pragma unroll
-      for (int g = 0; g < 8; ++g) d[g] = (uint32_t)wait_tag(w + g, e, t0, dead);
+      for (int g = 0; g < 8; ++g) d[g] = (uint32_t)wait_tag(w + g, e, t0, dead, s.wait_ns);
       uint4 lo, hi;
       lo.x = (d[0] & 0xffffu) | d[1] << 16;
       lo.y = (d[2] & 0xffffu) | d[3] << 16;
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(kRecvThreads) k_tp_recv(const __grid_constant_
         const uint64_t* w = words + ((long long)r * s.m + t) * s.n + c;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float f = __uint_as_float((uint32_t)wait_tag(w + j, e, t0, dead));
+          const float f = __uint_as_float((uint32_t)wait_tag(w + j, e, t0, dead, s.wait_ns));
           a[j] = r == 0 ? f : a[j] + f;
         }
       }
@@ -234,6 +235,7 @@ int mbp_tp_finish(int* const* flags, int rank, int P, int* counter, const void* 
   s.rank = rank;
   s.P = P;
   s.mode = mode;
+  s.wait_ns = wait_limit_ns();
   if (mode == MBP_TP_BARRIER) {
     if (!flags) return MBP_ERR_ARG;
     for (int r = 0; r < P; ++r) {

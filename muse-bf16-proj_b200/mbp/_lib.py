@@ -63,6 +63,7 @@ SIGNATURES = [
     ("mbp_version", _I, []),
     ("mbp_device_check", _I, [_I]),
     ("mbp_status", _I, [ctypes.POINTER(ctypes.c_int), _I]),
+    ("mbp_set_wait_limit", ctypes.c_ulonglong, [ctypes.c_ulonglong]),
     ("mbp_pack_c12_workspace", _SZ, [_I, _I]),
     ("mbp_pack_c12", _I, [_P, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),
     ("mbp_pack_c12_noalloc", _I, [_P, _I, _I, _I, _P, _P, _P, _P]),
@@ -87,8 +88,9 @@ SIGNATURES = [
                            _P]),
     ("mbp_gemv_c12_tp", _I, [ctypes.POINTER(C12), _P, _I, _I, ctypes.POINTER(TPExchange), _P, ctypes.POINTER(Geom),
                              _P]),
-    ("mbp_gemm_c12", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
-    ("mbp_gemm_c12_f32", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
+    ("mbp_gemm_workspace", _SZ, [_I, _I, _I]),
+    ("mbp_gemm_c12", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P, _SZ, _P]),
+    ("mbp_gemm_c12_f32", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P, _SZ, _P]),
 ]
 
 _lib = None
@@ -116,6 +118,12 @@ def lib():
 def check(rc: int, what: str) -> None:
     if rc != 0:
         raise MbpError(rc, what)
+
+
+def set_wait_limit(ns: int) -> int:
+    """Limit (ns) of every bounded device wait in kernels launched from now on (0: the default 1 s); returns the
+    previous one.  A wait that runs out sets its MBP_DEV_TIMEOUT_* code in the status word (``device_status``)."""
+    return int(lib().mbp_set_wait_limit(int(ns)))
 
 
 def device_status(clear: bool = True) -> int:

@@ -127,10 +127,14 @@ def _p2p_placement_ok(seen: list, host: str, local: dict, dev: int, can_access) 
     """The peer-store rule for one rank: `seen` = (hostname, GPU uuid) of every rank, `local` = uuid -> device
     index of the GPUs this process sees, `dev` = this rank's device index, `can_access(a, b)` = peer access.
     True only for at most 8 ranks on this host, each on a GPU of its own (waiting kernels of two ranks on one GPU
-    are not guaranteed to run at the same time), every peer visible here being peer-accessible."""
+    are not guaranteed to run at the same time), every peer's GPU visible to this process and peer-accessible
+    from this rank's GPU.  A peer this process cannot see (per-rank device lists) gives False: whether its
+    exchange buffer could be mapped through CUDA IPC is then unknown, and NCCL needs no such mapping."""
     if len(seen) > 8 or len({u for _, u in seen}) != len(seen) or any(h != host for h, _ in seen):
         return False
-    return all(can_access(dev, local[u]) for _, u in seen if u in local and local[u] != dev)
+    if any(u not in local for _, u in seen):
+        return False
+    return all(can_access(dev, local[u]) for _, u in seen if local[u] != dev)
 
 
 def _same_node(group) -> bool:
@@ -387,8 +391,21 @@ def release_tp(state: dict):
             sync.close()
 
 
+def check_exchange(clear: bool = True) -> None:
+    """Raises ``MbpError`` when a bounded wait of a peer-store exchange on this device gave up since the last
+    check (device status MBP_DEV_TIMEOUT_PEER: a peer's words or flags did not arrive within the wait limit, so
+    the outputs of the calls since then may hold stale or partial data).  The kernels never trap and the calls
+    themselves do not synchronise, so a caller that needs the guarantee calls this after synchronising a step
+    (``torch.cuda.synchronize()``), e.g. once per decode step or after a graph replay."""
+    from ._lib import DEVICE_STATUS, MbpError, device_status
+    st = device_status(clear)
+    if st:
+        raise MbpError(-200 - st, f"device status {st} ({DEVICE_STATUS.get(st, 'unknown')})")
+
+
 def kernel_fn_tp(data: dict, state: dict) -> torch.Tensor:
-    """``kernel_fn`` for P ranks: the full projection output (all-reduce / all-gather) on every rank."""
+    """``kernel_fn`` for P ranks: the full projection output (all-reduce / all-gather) on every rank.  Exchange
+    failures surface through the device status word, not here: see ``check_exchange``."""
     layer = data["config"]["layer"]
     x = data["x"]
     if not x.is_contiguous():

@@ -34,12 +34,13 @@ def test_gemm_onehot_exact():
     assert mbp.device_status() == 0
 
 
+@pytest.mark.parametrize("variant", ["plain", "esc1pct"])
 @pytest.mark.parametrize("layer", list(CONFIG3))
 @pytest.mark.parametrize("m", [128, 256])
-def test_gemm_baseline_config3(layer, m):
+def test_gemm_baseline_config3(layer, m, variant):
     import mbp
     n, k = CONFIG3[layer]
-    w = weight(n, k, seed=0)
+    w = weight(n, k, seed=0, escape_frac=0.01 if variant == "esc1pct" else 0.0)
     p = mbp.pack_c12(w)
     x = tokens(m, k, seed=m)
     out = mbp.gemm(p, x)
@@ -119,3 +120,41 @@ def test_gemm_repeated_calls_stage_reuse(shape):
     assert mbp.device_status() == 0
     for o in outs:
         assert torch.allclose(o, ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("m", [16, 32, 128, 256])
+def test_gemm_streamk_deterministic(m):
+    """Split tiles are summed by their last contributor in CTA order, so repeated calls give identical bits; the
+    whole-tile decomposition (no workspace) sums in another order and agrees to FP32 rounding."""
+    import mbp
+    w = weight(2048, 6144, seed=51, escape_frac=0.005)
+    p = mbp.pack_c12(w)
+    x = tokens(m, 6144, seed=52)
+    ref = ref_f32(x, w)
+    a = mbp.gemm(p, x, out_dtype=torch.float32)
+    b = mbp.gemm(p, x, out_dtype=torch.float32)
+    whole = mbp.gemm(p, x, out_dtype=torch.float32, workspace=torch.empty(0, dtype=torch.uint8, device="cuda"))
+    torch.cuda.synchronize()
+    assert mbp.device_status() == 0
+    assert torch.equal(a, b)
+    assert torch.allclose(a, whole, rtol=1e-4, atol=1e-3)
+    assert torch.allclose(a, ref, rtol=1e-3, atol=1e-2)
+    assert_close_bf16(mbp.gemm(p, x), ref)
+
+
+@pytest.mark.parametrize("layer", ["qkv_gate", "o"])
+@pytest.mark.parametrize("m", [9, 16, 24, 32])
+@pytest.mark.parametrize("variant", ["plain", "esc1pct"])
+def test_gemm_decode_shapes(layer, m, variant):
+    """The decode shapes at the token counts the tensor-core path may take."""
+    import mbp
+    n, k = CONFIG3[layer]
+    w = weight(n, k, seed=0, escape_frac=0.01 if variant == "esc1pct" else 0.0)
+    p = mbp.pack_c12(w)
+    x = tokens(m, k, seed=m)
+    out = mbp.gemm(p, x)
+    torch.cuda.synchronize()
+    assert mbp.device_status() == 0
+    ref = ref_f32(x, w)
+    assert_close_bf16(out, ref)
+    assert_reference_norms(out, ref)

@@ -160,5 +160,5 @@ def test_peer_store_placement_rule():
     assert not _p2p_placement_ok(seen(["GPU-0", "GPU-1"], {1: "other"}), "h", local, 0, peers)  # two hosts
     assert not _p2p_placement_ok(seen([f"GPU-{i}" for i in range(9)]), "h", dict(local, **{"GPU-8": 8}), 0, peers)
     assert not _p2p_placement_ok(seen(["GPU-0", "GPU-1"]), "h", local, 0, lambda a, b: False)  # no peer access
-    # a peer this process cannot see (per-rank device lists) is not asked about
-    assert _p2p_placement_ok(seen(["GPU-0", "GPU-5"]), "h", {"GPU-0": 0}, 0, lambda a, b: False)
+    # a peer this process cannot see (per-rank device lists): its buffer's IPC mapping is unknown, so NCCL
+    assert not _p2p_placement_ok(seen(["GPU-0", "GPU-5"]), "h", {"GPU-0": 0}, 0, peers)
