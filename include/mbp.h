@@ -149,10 +149,11 @@ int mbp_gemv_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, floa
  * out[m, n_out] = x . W[0:n_out]^T, FP32 accumulation in TMEM, any m >= 1 (token tiles of up to 256).
  * The work is split evenly over the SMs (stream-K): parts of split tiles go through `workspace` as FP32 partial
  * tiles and the last contributor of a tile adds them in a fixed order (results do not depend on timing).
- * workspace: mbp_gemm_workspace(n_out, k, m) bytes, 256-byte aligned, ZERO-FILLED before its first use (the
- * calls leave its tickets at zero again); calls that share a workspace must be ordered on one stream.  NULL (or
- * too small) runs one whole tile per CTA instead, which leaves SMs idle when the tile count is not a multiple of
- * the SM count. ---- */
+ * workspace: mbp_gemm_workspace(n_out, k, m) bytes, 256-byte aligned, ZERO-FILLED before its first use: its first
+ * 64 KiB hold one ticket per tile, which every call leaves at zero again, so one workspace serves calls of any
+ * shape (the largest size they need); calls that share a workspace must be ordered on one stream.  NULL (or too
+ * small) runs one whole tile per CTA instead, which leaves SMs idle when the tile count is not a multiple of the
+ * SM count. ---- */
 size_t mbp_gemm_workspace(int n_out, int k, int m);
 int mbp_gemm_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo, void* workspace,
                  size_t workspace_bytes, cudaStream_t stream);

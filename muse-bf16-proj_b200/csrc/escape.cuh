@@ -49,6 +49,12 @@ struct EscCursor {
     win0 = load(begin, lane);
     win1 = load(begin + 32, lane);
     next_chunk = esc_chunk(__shfl_sync(0xffffffffu, win0, 0));
+    // The rest of the slice goes to L2 now: a window is loaded only one window (a few units of work) ahead of its
+    // use, less than the latency of a cold HBM read while the weights stream.  Only the whole 16-byte blocks
+    // inside the slice (a bulk prefetch needs 16-byte alignment), so it never touches memory outside the list.
+    const uintptr_t pb = ((uintptr_t)(esc + begin + 64) + 15u) & ~(uintptr_t)15u;
+    const uintptr_t pe = (uintptr_t)(esc + end) & ~(uintptr_t)15u;
+    if (lane == 0 && end - begin > 64 && pe > pb) prefetch_l2(reinterpret_cast<const void*>(pb), (uint32_t)(pe - pb));
   }
 
   // Skips the entries of chunks below c (chunks this warp does not process).  Warp-uniform.

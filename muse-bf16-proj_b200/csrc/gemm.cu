@@ -57,6 +57,7 @@ constexpr int kEpiBar = 2;                 // named barrier of the 4 epilogue wa
 constexpr int kPackedStage = 8 * MBP_C12_UNIT_BYTES;  // 12 KB
 constexpr int kAStage = 128 * 128;                    // 128 rows x 64 bf16
 constexpr int kMaxSmem = 227 * 1024;
+constexpr int kMaxParts = 8;               // contributors of one split tile (the host's plan keeps to it)
 static_assert(kEpi0 % 4 == 0, "epilogue warp kEpi0 + q must own TMEM lane quadrant q");
 
 struct __align__(64) GemmParams {
@@ -99,9 +100,15 @@ struct Cfg {
   static_assert(kSmem <= kMaxSmem, "shared memory");
 };
 
-using CfgS = Cfg<12, 2, 4, 32>;  // <= 32 tokens: deep weight ring
-using CfgM = Cfg<8, 2, 4, 128>;  // <= 128 tokens
-using CfgL = Cfg<6, 2, 3, 256>;  // <= 256 tokens
+// Instances (ring depths per token-tile class); pick() chooses one per call.
+using CfgS0 = Cfg<12, 2, 4, 32>;
+using CfgS1 = Cfg<10, 4, 4, 32>;
+using CfgS2 = Cfg<8, 6, 4, 32>;
+using CfgM0 = Cfg<8, 2, 4, 128>;
+using CfgM1 = Cfg<6, 4, 3, 128>;
+using CfgL0 = Cfg<6, 2, 3, 256>;
+using CfgL1 = Cfg<4, 4, 3, 256>;
+using CfgL2 = Cfg<6, 4, 2, 256>;
 
 MBP_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
   asm volatile(
@@ -444,34 +451,62 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       named_bar_sync(kEpiBar, 128);
       if (*ticket_word == c_hi - c_lo) {
         __threadfence();
-        // float4 f = rows 4*(f % 32) .. +3 of column f / 32: a warp reads one column's 128 rows per step
-        const int ncols = min(p.bn, p.m - tok0);
-        for (int f = et; f < ncols * 32; f += 128) {
-          const int col = f >> 5, r4 = (f & 31) * 4;
-          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int c2 = c_lo; c2 <= c_hi; ++c2) {
-            const int which = range_start(c2, p.U, G) >= t0 ? 0 : 1;  // the tile is c2's first or last segment
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(
-                p.ws_part + (size_t)(2 * c2 + which) * slot_elems + (size_t)col * 128 + r4));
-            sum.x += v.x;
-            sum.y += v.y;
-            sum.z += v.z;
-            sum.w += v.w;
+        // float4 f = rows 4*(f % 32) .. +3 of column f / 32: a warp reads one column's 128 rows per step.  The
+        // contributors are CTAs c_lo..c_hi; the tile is the first segment of each of them but c_lo, whose range may
+        // start in an earlier tile (then the tile is its last segment).  Loads of two contributors for two
+        // float4s are issued together (L2-resident partials), then added in CTA order.
+        const int ncols = min(p.bn, p.m - tok0), nf = ncols * 32;
+        const int lo_which = range_start(c_lo, p.U, G) >= t0 ? 0 : 1;
+        const float* part0 = p.ws_part + (size_t)(2 * c_lo + lo_which) * slot_elems;  // c_lo's slot
+        const float* part1 = p.ws_part + (size_t)(2 * (c_lo + 1)) * slot_elems;       // c_lo + 1 + i: part1 + 2i slots
+        for (int f0 = et; f0 < nf; f0 += 2 * 128) {
+          float4 sum[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int f = min(f0 + u * 128, nf - 1);
+            sum[u] = __ldcg(reinterpret_cast<const float4*>(part0 + (size_t)(f >> 5) * 128 + (f & 31) * 4));
           }
-          const int grow = rb * 128 + r4;  // Rout * 16 is a multiple of 16: four rows are all in or all out
-          if (grow < p.Rout * 16 && !p.vec_out) {
-            store_elem(p, tok0 + col, grow, sum.x);
-            store_elem(p, tok0 + col, grow + 1, sum.y);
-            store_elem(p, tok0 + col, grow + 2, sum.z);
-            store_elem(p, tok0 + col, grow + 3, sum.w);
-          } else if (grow < p.Rout * 16) {
-            if (p.f32out) {
-              *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)(tok0 + col) * p.ldo + grow) = sum;
+          for (int i0 = 0; i0 < c_hi - c_lo; i0 += 2) {
+            float4 v[2][2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int f = min(f0 + u * 128, nf - 1);
+#pragma unroll
+              for (int i = 0; i < 2; ++i)
+                if (i0 + i < c_hi - c_lo)
+                  v[u][i] = __ldcg(reinterpret_cast<const float4*>(part1 + (size_t)(2 * (i0 + i)) * slot_elems +
+                                                                   (size_t)(f >> 5) * 128 + (f & 31) * 4));
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+#pragma unroll
+              for (int i = 0; i < 2; ++i)
+                if (i0 + i < c_hi - c_lo) {
+                  sum[u].x += v[u][i].x;
+                  sum[u].y += v[u][i].y;
+                  sum[u].z += v[u][i].z;
+                  sum[u].w += v[u][i].w;
+                }
+          }
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int f = f0 + u * 128;
+            if (f >= nf) break;
+            const int col = f >> 5, grow = rb * 128 + (f & 31) * 4;
+            // Rout * 16 is a multiple of 16: four rows are all in or all out
+            if (grow >= p.Rout * 16) continue;
+            if (!p.vec_out) {
+              store_elem(p, tok0 + col, grow, sum[u].x);
+              store_elem(p, tok0 + col, grow + 1, sum[u].y);
+              store_elem(p, tok0 + col, grow + 2, sum[u].z);
+              store_elem(p, tok0 + col, grow + 3, sum[u].w);
+            } else if (p.f32out) {
+              *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)(tok0 + col) * p.ldo + grow) = sum[u];
             } else {
-              const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(sum.x)) |
-                                  (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(sum.y)) << 16;
-              const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(sum.z)) |
-                                  (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(sum.w)) << 16;
+              const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(sum[u].x)) |
+                                  (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(sum[u].y)) << 16;
+              const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(sum[u].z)) |
+                                  (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(sum[u].w)) << 16;
               *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.out) + (size_t)(tok0 + col) * p.ldo + grow) =
                   make_uint2(lo, hi);
             }
@@ -512,18 +547,34 @@ KernelFn kernel_of() {
   return reinterpret_cast<KernelFn>(&k_gemm<CF>);
 }
 
+template <class CF>
+KernelFn inst(int* smem) {
+  *smem = CF::kSmem;
+  return kernel_of<CF>();
+}
+
 // The instance for a token tile of bn tokens (bn % 16 == 0, <= 256) and its shared-memory request.
+// MBP_GEMM_CFG=<i> selects the i-th instance of the class (ring-depth sweeps).
 KernelFn pick(int bn, int* smem) {
-  if (bn <= CfgS::kBNMax) {
-    *smem = CfgS::kSmem;
-    return kernel_of<CfgS>();
+  static const int sel = getenv("MBP_GEMM_CFG") ? atoi(getenv("MBP_GEMM_CFG")) : -1;
+  if (bn <= 32) {
+    switch (sel) {
+      case 0: return inst<CfgS0>(smem);
+      case 2: return inst<CfgS2>(smem);
+      default: return inst<CfgS1>(smem);
+    }
   }
-  if (bn <= CfgM::kBNMax) {
-    *smem = CfgM::kSmem;
-    return kernel_of<CfgM>();
+  if (bn <= 128) {
+    switch (sel) {
+      case 0: return inst<CfgM0>(smem);
+      default: return inst<CfgM1>(smem);
+    }
   }
-  *smem = CfgL::kSmem;
-  return kernel_of<CfgL>();
+  switch (sel) {
+    case 0: return inst<CfgL0>(smem);
+    case 2: return inst<CfgL2>(smem);
+    default: return inst<CfgL1>(smem);
+  }
 }
 
 std::mutex g_mu;
@@ -568,7 +619,8 @@ Plan make_plan(int n_out, int k, int m, int sms, bool streamk) {
     // One CTA per SM, each with at least C / (parts - 1) items, so that a tile has at most `parts` contributors
     // and the last one's fix-up (it re-reads the others' partial tiles) stays short: FP32 partials of wide token
     // tiles are large, so those get fewer parts.
-    const int parts = pl.bn <= 64 ? 8 : 4;
+    static const int parts_env = getenv("MBP_GEMM_PARTS") ? atoi(getenv("MBP_GEMM_PARTS")) : 0;
+    const int parts = parts_env >= 2 && parts_env <= kMaxParts ? parts_env : pl.bn <= 64 ? 8 : 4;
     const long long min_items = (C + parts - 2) / (parts - 1);
     G = pl.U / min_items;
     if (G > sms) G = sms;
@@ -582,11 +634,15 @@ Plan make_plan(int n_out, int k, int m, int sms, bool streamk) {
   return pl;
 }
 
-// Workspace of a stream-K plan: tickets (one int per tile, 256-byte padded) + two partial-tile slots per CTA.
+// Workspace of a stream-K plan: a fixed region of tickets (one int per tile) that every shape places at the same
+// offset -- a workspace shared by calls of different shapes must never see one call's partial tiles land on
+// another call's tickets -- then two partial-tile slots per CTA.
+constexpr int kMaxTickets = 16384;
+constexpr size_t kTicketBytes = (size_t)kMaxTickets * 4;
+
 size_t ws_bytes_for(const Plan& pl) {
   if (pl.G == pl.tiles) return 0;  // every CTA takes exactly one whole tile
-  const size_t cnt = ((size_t)pl.tiles * 4 + 255) & ~(size_t)255;
-  return cnt + (size_t)2 * pl.G * pl.bn * 128 * 4;
+  return kTicketBytes + (size_t)2 * pl.G * pl.bn * 128 * 4;
 }
 
 int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out, int ldo, bool f32, void* ws,
@@ -598,18 +654,22 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   if (ldo < n_out) return MBP_ERR_SHAPE;
   if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u) || ((uintptr_t)ws & 255u)) return MBP_ERR_ALIGN;
   const int sms = sm_count();
-  Plan pl = make_plan(n_out, w->k, m, sms, true);
+  static const bool no_split = getenv("MBP_GEMM_PARTS") && atoi(getenv("MBP_GEMM_PARTS")) == 1;
+  Plan pl = make_plan(n_out, w->k, m, sms, !no_split);
   if (pl.U > 0x7fffffffLL / 2) return MBP_ERR_SHAPE;  // items are indexed with 32-bit integers
-  if (!ws || ws_bytes < ws_bytes_for(pl)) pl = make_plan(n_out, w->k, m, sms, false);  // no workspace: whole tiles
+  // no (or a too small) workspace, or more tiles than tickets: whole tiles per CTA
+  if (!ws || ws_bytes < ws_bytes_for(pl) || pl.tiles > kMaxTickets) pl = make_plan(n_out, w->k, m, sms, false);
   int smem = 0;
   const KernelFn fn = pick(pl.bn, &smem);
   int rc = ensure_attr(fn, smem);
   if (rc) return rc;
   GemmParams p;
   const int R = w->n / 16, C = w->k / 64;
-  if (!encode_units_3d(&p.wmap, w->units, R, C)) return MBP_ERR_TMAP;
-  if (!encode_bf16_2d(&p.xmap, x, (uint64_t)m, (uint64_t)w->k, (uint64_t)w->k, (uint32_t)pl.bn, 64u,
-                      CU_TENSOR_MAP_SWIZZLE_128B))
+  const TmapKey wkey{w->units, (uint64_t)R, (uint64_t)C, 0, 0, 0, 0x200u};
+  if (!cached_map(&p.wmap, wkey, [&](CUtensorMap* mp) { return encode_units_3d(mp, w->units, R, C); }))
+    return MBP_ERR_TMAP;
+  if (!encode_bf16_2d_cached(&p.xmap, x, (uint64_t)m, (uint64_t)w->k, (uint64_t)w->k, (uint32_t)pl.bn, 64u,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
     return MBP_ERR_TMAP;
   p.units = w->units;
   p.bases = w->bases;
@@ -617,9 +677,8 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   p.esc = w->esc;
   p.out = out;
   const bool split = pl.G != pl.tiles;
-  const size_t cnt = ((size_t)pl.tiles * 4 + 255) & ~(size_t)255;
   p.ws_cnt = split ? static_cast<int*>(ws) : nullptr;
-  p.ws_part = split ? reinterpret_cast<float*>(static_cast<char*>(ws) + cnt) : nullptr;
+  p.ws_part = split ? reinterpret_cast<float*>(static_cast<char*>(ws) + kTicketBytes) : nullptr;
   p.U = pl.U;
   p.C = C;
   p.Rout = n_out / 16;

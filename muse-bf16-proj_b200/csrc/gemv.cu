@@ -73,6 +73,7 @@ struct __align__(64) GemvParams {
   int rb, split, wki, kci, stages;
   int nblk;     // row blocks: block b owns row tiles [b*Rout/nblk, (b+1)*Rout/nblk), at most rb of them
   int has_esc;  // the matrix has escapes: consumer warps get escape masks
+  int pre_stages;  // pipeline stages whose weights are prefetched into L2 before the dependency wait
   unsigned long long wait_ns;  // limit of every bounded wait
 };
 
@@ -287,7 +288,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   }
   if (warp == nwc) {
     if (lane == 0) prefetch_tmap(&p.xmap);
-    const int per_it = rvalid * p.wki, npre = min(p.stages, nit) * per_it;
+    const int per_it = rvalid * p.wki, npre = min(p.pre_stages, nit) * per_it;
     for (int i = lane; i < npre; i += 32) {
       const int it = i / per_it, rr = (i - it * per_it) / p.wki, q = i - it * per_it - rr * p.wki;
       const int c0 = cs + q * Lk + it * p.kci, e = min(cs + (q + 1) * Lk, ce);
@@ -960,8 +961,8 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
                   max_ctas(fn, g.split, 32 * (rows_w * g.wki + 1), smem_request(L)))
     return MBP_ERR_SPLIT;
   GemvParams p;
-  if (!encode_bf16_2d(&p.xmap, x, (uint64_t)m, (uint64_t)K, (uint64_t)ldx, (uint32_t)tok, 64u,
-                      CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!encode_bf16_2d_cached(&p.xmap, x, (uint64_t)m, (uint64_t)K, (uint64_t)ldx, (uint32_t)tok, 64u,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
     return MBP_ERR_TMAP;
   p.units = units;
   p.bases = bases;
@@ -988,6 +989,8 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   p.nblk = nblk;
   p.has_esc = with_esc ? 1 : 0;
   p.wait_ns = wait_limit_ns();
+  static const int pre_env = getenv("MBP_GEMV_PREFETCH") ? atoi(getenv("MBP_GEMV_PREFETCH")) : 0;
+  p.pre_stages = pre_env > 0 ? pre_env : g.stages;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nblk, g.split, (m + tok - 1) / tok);
   cfg.blockDim = dim3(32 * (rows_w * g.wki + 1));

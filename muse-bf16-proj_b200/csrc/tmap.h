@@ -36,4 +36,48 @@ inline bool encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, ui
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Per-thread cache of encoded maps (a direct-mapped table keyed by every argument of the encode): a serving loop
+// calls with the same few x buffers and weights over and over, and encoding costs about a microsecond of host
+// time per call.  A stale entry is impossible: the key is the full description of the map, including the base.
+struct TmapKey {
+  const void* base;
+  uint64_t a, b, c;
+  uint32_t d, e, kind;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && a == o.a && b == o.b && c == o.c && d == o.d && e == o.e && kind == o.kind;
+  }
+};
+
+template <class Encode>
+inline bool cached_map(CUtensorMap* map, const TmapKey& key, Encode&& encode) {
+  constexpr int kSlots = 64;
+  struct Slot {
+    TmapKey key;
+    CUtensorMap map;
+    bool used;
+  };
+  static thread_local Slot slots[kSlots] = {};
+  const uintptr_t h = (reinterpret_cast<uintptr_t>(key.base) >> 8) ^ (key.a * 131u) ^ (key.c * 7u) ^ key.d ^
+                      (key.kind << 5);
+  Slot& s = slots[h % kSlots];
+  if (s.used && s.key == key) {
+    *map = s.map;
+    return true;
+  }
+  if (!encode(map)) return false;
+  s.key = key;
+  s.map = *map;
+  s.used = true;
+  return true;
+}
+
+// encode_bf16_2d through the cache.
+inline bool encode_bf16_2d_cached(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                                  uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swz) {
+  const TmapKey key{base, rows, cols, ld, box_rows, box_cols, 0x100u | (uint32_t)swz};
+  return cached_map(map, key, [&](CUtensorMap* m) {
+    return encode_bf16_2d(m, base, rows, cols, ld, box_rows, box_cols, swz);
+  });
+}
+
 }  // namespace mbp

@@ -15,12 +15,18 @@ from ._lib import C12, Geom, HiLo, check, lib
 BASE_MATRIX, BASE_TILE = 0, 1
 
 
-def _stream():
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream(device: torch.device | None = None):
+    """The current CUDA stream of `device` (default: the current device) as a raw handle for the C ABI."""
+    if _raw_stream is not None:
+        return _raw_stream(torch.cuda.current_device() if device is None or device.index is None else device.index)
+    return torch.cuda.current_stream(device).cuda_stream
 
 
 def _ptr(t: torch.Tensor | None):
-    return ctypes.c_void_p(t.data_ptr() if t is not None and t.numel() else 0)
+    return t.data_ptr() if t is not None and t.numel() else None
 
 
 @dataclass
@@ -156,8 +162,8 @@ def gemv(p: PackedC12, x: torch.Tensor, n_out: int | None = None, out: torch.Ten
     fn = lib().mbp_gemv_c12_f32 if out.dtype == torch.float32 else lib().mbp_gemv_c12
     if out.dtype not in (torch.float32, torch.bfloat16):
         raise ValueError(f"unsupported output dtype {out.dtype}")
-    check(fn(ctypes.byref(p.desc), _ptr(x), m, n_out, _ptr(out), out.stride(0),
-             ctypes.byref(geom) if geom is not None else None, _stream()), "mbp_gemv_c12")
+    check(fn(ctypes.byref(p.desc), x.data_ptr(), m, n_out, out.data_ptr(), out.stride(0),
+             ctypes.byref(geom) if geom is not None else None, _stream(x.device)), "mbp_gemv_c12")
     return out
 
 
@@ -170,7 +176,7 @@ def gemm_workspace(n_out: int, k: int, m: int, device=None) -> torch.Tensor:
     calls on different streams get different workspaces."""
     nbytes = int(lib().mbp_gemm_workspace(n_out, k, m))
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    key = (dev.index, _stream(dev))
     ws = _WORKSPACES.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
@@ -195,8 +201,8 @@ def gemm(p: PackedC12, x: torch.Tensor, n_out: int | None = None, out: torch.Ten
     if workspace is None:
         workspace = gemm_workspace(n_out, p.k, m, x.device)
     fn = lib().mbp_gemm_c12_f32 if out.dtype == torch.float32 else lib().mbp_gemm_c12
-    check(fn(ctypes.byref(p.desc), _ptr(x), m, n_out, _ptr(out), out.stride(0), _ptr(workspace), workspace.numel(),
-             _stream()), "mbp_gemm_c12")
+    check(fn(ctypes.byref(p.desc), x.data_ptr(), m, n_out, out.data_ptr(), out.stride(0), _ptr(workspace),
+             workspace.numel(), _stream(x.device)), "mbp_gemm_c12")
     return out
 
 
@@ -206,8 +212,9 @@ def router(p: PackedHiLo, x: torch.Tensor, out: torch.Tensor | None = None, geom
     m = x.shape[0]
     if out is None:
         out = torch.empty((m, p.n), dtype=torch.float32, device=x.device)
-    check(lib().mbp_router_hilo(ctypes.byref(p.desc), _ptr(x), m, _ptr(out), out.stride(0),
-                                ctypes.byref(geom) if geom is not None else None, _stream()), "mbp_router_hilo")
+    check(lib().mbp_router_hilo(ctypes.byref(p.desc), x.data_ptr(), m, out.data_ptr(), out.stride(0),
+                                ctypes.byref(geom) if geom is not None else None, _stream(x.device)),
+          "mbp_router_hilo")
     return out
 
 

@@ -158,3 +158,23 @@ def test_gemm_decode_shapes(layer, m, variant):
     ref = ref_f32(x, w)
     assert_close_bf16(out, ref)
     assert_reference_norms(out, ref)
+
+
+def test_gemm_workspace_shared_across_shapes():
+    """One workspace serves calls of different shapes in any order: wide token tiles (large partial tiles) and
+    then a shape with many tiles, whose tickets must still start at zero; every call leaves the tickets zero."""
+    import mbp
+    from mbp.ops import gemm_workspace
+    a = weight(2048, 6144, seed=61)
+    b = weight(14336, 6144, seed=62)
+    pa, pb = mbp.pack_c12(a), mbp.pack_c12(b)
+    for m_a, m_b in ((256, 9), (128, 16), (256, 32)):
+        xa, xb = tokens(m_a, 6144, seed=m_a), tokens(m_b, 6144, seed=m_b + 1)
+        oa = mbp.gemm(pa, xa)
+        ob = mbp.gemm(pb, xb)
+        torch.cuda.synchronize()
+        assert mbp.device_status() == 0
+        assert_close_bf16(oa, ref_f32(xa, a))
+        assert_close_bf16(ob, ref_f32(xb, b))
+    ws = gemm_workspace(14336, 6144, 9)
+    assert int(ws[: 64 * 1024].view(torch.int32).abs().sum()) == 0
