@@ -17,16 +17,19 @@
 // another.  Without a workspace every CTA takes one whole tile.
 //
 // Warp roles (24 warps):
-//   warp 0       TMA producer of the weights: one 3-D box of the 8 packed units of an item (12 KB) per stage,
-//                PS stages deep (PS = 12 for <= 32 tokens: ~144 KB in flight per SM);
+//   warp 0       producer of the weights: a stage holds KC consecutive items, lanes 0-7 each fill their row
+//                tile's KC packed units (contiguous) with one TMA bulk copy, PS stages deep;
 //   warp 18      TMA producer of x: one 2-D box (BN rows x 128 bytes, 128-byte swizzle) per item;
 //   warp 19      MMA scheduler: waits for an item's decoded-A and x stages (and, at a segment start, for the
 //                epilogue to release the accumulator) and hands the item to the issuer on a named barrier;
-//   warp 1       allocates TMEM (two accumulators); lane 0 issues tcgen05.mma (M=128, N=BN, K=16) x4 per item
-//                and commits the stages back to their producers and finished segments to the epilogue;
-//   warps 2-17   decoders in two groups of 8 warps taking alternate items; warp d of a group decodes row tile d
-//                (12-bit decode and escape restoration in registers, as in the GEMV) into the canonical SW128
-//                K-major layout of the A stage and fences it to the async proxy;
+//   warp 1       allocates TMEM (accumulators, and the decoded-A ring); lane 0 issues tcgen05.mma (M=128, N=BN,
+//                K=16) x4 per item and commits the stages back to their producers and finished segments to the
+//                epilogue;
+//   warps 2-17   decoders in two groups of 8 warps taking alternate items; each warp decodes one row tile (12-bit
+//                decode and escape restoration in registers, as in the GEMV) and writes it as the MMA's A operand:
+//                into TMEM with tcgen05.st (the instances used; A then never touches shared memory, whose
+//                bandwidth otherwise bounds the 256-token tiles), or into the canonical SW128 K-major layout of a
+//                shared-memory A stage;
 //   warps 20-23  epilogue: warp 20+q reads TMEM lanes 32q..32q+31 (tcgen05.ld 32x32b), stores the tile or its
 //                partial and releases the accumulator, while the next segment's MMAs run in the other one.
 // All waits are bounded (status word, no trap); TMEM is always released.
@@ -54,14 +57,12 @@ constexpr int kEpi0 = kSchedWarp + 1;      // 20 (a multiple of 4: warp kEpi0 + 
 constexpr int kThreads = 32 * (kEpi0 + 4);
 constexpr int kHandBar = 1;                // named barrier: scheduler -> issuer hand-over (64 threads)
 constexpr int kEpiBar = 2;                 // named barrier of the 4 epilogue warps (128 threads)
-constexpr int kPackedStage = 8 * MBP_C12_UNIT_BYTES;  // 12 KB
 constexpr int kAStage = 128 * 128;                    // 128 rows x 64 bf16
 constexpr int kMaxSmem = 227 * 1024;
 constexpr int kMaxParts = 8;               // contributors of one split tile (the host's plan keeps to it)
 static_assert(kEpi0 % 4 == 0, "epilogue warp kEpi0 + q must own TMEM lane quadrant q");
 
 struct __align__(64) GemmParams {
-  CUtensorMap wmap;  // units as [R][C][192 x u64], box {192, 1, 8}
   CUtensorMap xmap;  // x [m, k] bf16, box {64 columns, bn rows}, 128-byte swizzle
   const uint8_t* units;
   const uint8_t* bases;
@@ -73,50 +74,49 @@ struct __align__(64) GemmParams {
   long long U;     // items = tiles * C
   int C, Rout, R8, m, ldo, bn, f32out;
   int vec_out;     // out and ldo allow 4-row vector stores (16-byte aligned base, ldo % 8 == 0)
-  int tcols;       // TMEM columns allocated (two accumulators of tcols / 2)
+  int tcols;       // TMEM columns allocated
+  int acc_cols;    // columns of one accumulator (>= bn, a multiple of 32)
   unsigned long long wait_ns;  // limit of every bounded wait
 };
 
-// Shared-memory layout of one instance: PS packed stages, AS decoded-A stages, XS x stages of up to BNMAX tokens.
-template <int PS, int AS, int XS, int BNMAX>
+// Layout of one instance: PS weight stages of KC items each (8 row tiles x KC consecutive packed units, filled
+// by one bulk copy of KC units per row tile), AS decoded-A stages (TA: in TMEM, 32 columns each after the
+// accumulators; else in shared memory), XS x stages of up to BNMAX tokens, NACC TMEM accumulators (2 lets a
+// segment's epilogue overlap the next segment's MMAs).
+template <int PS, int KC, int AS, int XS, int BNMAX, bool TA, int NACC>
 struct Cfg {
-  static constexpr int kPS = PS, kAS = AS, kXS = XS, kBNMax = BNMAX;
+  static constexpr int kPS = PS, kKC = KC, kAS = AS, kXS = XS, kBNMax = BNMAX, kNAcc = NACC;
+  static constexpr bool kTA = TA;
+  static constexpr int kPackedStage = 8 * KC * MBP_C12_UNIT_BYTES;
   static constexpr int kXStage = BNMAX * 128;
   static constexpr int kPacked = 0;
   static constexpr int kA = kPacked + PS * kPackedStage;  // multiples of 1024 (SW128 atoms)
-  static constexpr int kX = kA + AS * kAStage;
+  static constexpr int kX = kA + (TA ? 0 : AS * kAStage);
   static constexpr int kMask = kX + XS * kXStage;
   static constexpr int kBars = kMask + kDecWarps * kMaskUnitBytes;
   // pfull/pempty[PS], afull/aempty[AS], xfull/xempty[XS], accfull/accempty[2]
   static constexpr int kMisc = kBars + 8 * (2 * PS + 2 * AS + 2 * XS + 4);
   static constexpr int kTotal = kMisc + 16;    // TMEM base, abort word, ticket
   static constexpr int kSmem = kTotal + 1024;  // + alignment slack
-  // Stage ownership: decoder group g takes items g (mod kGroups).  A ring whose barriers the decoders wait on must
-  // give every stage to a single group (depth a multiple of kGroups): otherwise a group could wait for use k+1 of
-  // a stage while use k, owned by the other group and completed out of order by the TMA engine, is still pending,
-  // and mbarrier parity waits, which only tell the current phase from the previous one, would return on the stale
-  // phase.
-  static_assert(PS % kGroups == 0 && AS % kGroups == 0, "ring depths must be multiples of the decoder groups");
+  // Stage ownership: decoder group g takes items g (mod kGroups).  A ring whose barriers only one group waits on
+  // per use must give every stage to a single group (depth a multiple of kGroups): otherwise a group could wait for
+  // use k+1 of a stage while use k, owned by the other group and completed out of order by the TMA engine, is
+  // still pending, and mbarrier parity waits, which only tell the current phase from the previous one, would
+  // return on the stale phase.  The decoded-A ring is such a ring; every decoder warp waits on and releases every
+  // use of a weight stage, so that ring may have any depth.
+  static_assert(AS % kGroups == 0, "the decoded-A ring depth must be a multiple of the decoder groups");
   static_assert(kSmem <= kMaxSmem, "shared memory");
 };
 
 // Instances (ring depths per token-tile class); pick() chooses one per call.
-using CfgS0 = Cfg<12, 2, 4, 32>;
-using CfgS1 = Cfg<10, 4, 4, 32>;
-using CfgS2 = Cfg<8, 6, 4, 32>;
-using CfgM0 = Cfg<8, 2, 4, 128>;
-using CfgM1 = Cfg<6, 4, 3, 128>;
-using CfgL0 = Cfg<6, 2, 3, 256>;
-using CfgL1 = Cfg<4, 4, 3, 256>;
-using CfgL2 = Cfg<6, 4, 2, 256>;
-
-MBP_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(dst),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
-      : "memory");
-}
+using CfgS0 = Cfg<3, 4, 2, 4, 32, false, 2>;
+using CfgS1 = Cfg<3, 4, 4, 4, 32, true, 2>;
+using CfgS2 = Cfg<4, 4, 8, 4, 32, true, 2>;
+using CfgM0 = Cfg<2, 4, 2, 4, 128, false, 2>;
+using CfgM1 = Cfg<3, 4, 4, 4, 128, true, 2>;
+using CfgL0 = Cfg<3, 2, 2, 3, 256, false, 2>;
+using CfgL1 = Cfg<2, 4, 4, 3, 256, true, 1>;
+using CfgL2 = Cfg<3, 2, 8, 3, 256, true, 1>;
 
 MBP_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 MBP_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -139,6 +139,28 @@ MBP_DEV void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uin
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
+}
+
+// A from TMEM (M=128 lanes = rows, 8 columns per K=16: a column holds two consecutive K elements, low half first).
+MBP_DEV void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// 16 lanes x 32 columns from the mma.sync A-fragment registers of a decoded unit: in the .16x128b shape thread
+// 4g + t holds (lane g, column t) and (lane g + 8, column t) of each 4-column block, and .x8 repeats the block
+// along the columns with the next register pair -- A[4q], A[4q+1] (k pairs t of step q) then A[4q+2], A[4q+3]
+// (k pairs t + 4) -- so the sixteen registers land as 16 rows x 64 K in order.
+MBP_DEV void tc_st_a(uint32_t taddr, const uint32_t (&a)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x128b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]), "r"(a[8]), "r"(a[9]),
+      "r"(a[10]), "r"(a[11]), "r"(a[12]), "r"(a[13]), "r"(a[14]), "r"(a[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 MBP_DEV void tc_commit(uint32_t bar) {
@@ -181,7 +203,8 @@ MBP_DEV Seg seg_of(int tile, int u0, int u1, int C) {
 
 template <class CF>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ GemmParams p) {
-  constexpr int PS = CF::kPS, AS = CF::kAS, XS = CF::kXS;
+  constexpr int PS = CF::kPS, KC = CF::kKC, AS = CF::kAS, XS = CF::kXS, NACC = CF::kNAcc;
+  constexpr int kPackedStage = CF::kPackedStage;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -202,17 +225,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   const int nit = u1 - u0;
   const int tile_first = u0 / C, tile_last = (u1 - 1) / C;
   const int nseg = tile_last - tile_first + 1;
-  const uint32_t acc_cols = (uint32_t)p.tcols / 2;
+  const uint32_t acc_cols = (uint32_t)p.acc_cols;
+  const uint32_t a_col0 = NACC * acc_cols;  // TMEM-resident A ring (CF::kTA): AS stages of 32 columns
 
   // Programmatic dependent launch: the packed weights never depend on the previous kernel of the stream, so the
   // first stages' units are pulled into L2 while it drains; every thread waits for it before touching x or out.
-  if (warp == kWProdWarp) {
-    for (int i = lane; i < 8 * min(PS, nit); i += 32) {
-      const int u = u0 + (i >> 3);
-      const int tile = u / C, chunk = u - tile * C;
-      const int rt = (tile % p.R8) * 8 + (i & 7);
-      if (rt < p.Rout) prefetch_l2(p.units + ((size_t)rt * C + chunk) * MBP_C12_UNIT_BYTES, MBP_C12_UNIT_BYTES);
-    }
+  if (warp == kWProdWarp && lane < 8) {  // the first weight stages' units, one contiguous run per row tile
+    const Seg sg = seg_of(tile_first, u0, u1, C);
+    const int rt = (sg.tile % p.R8) * 8 + lane, n = min(PS * KC, sg.ce - sg.cb);
+    if (rt < p.Rout) prefetch_l2(p.units + ((size_t)rt * C + sg.cb) * MBP_C12_UNIT_BYTES, (uint32_t)n * MBP_C12_UNIT_BYTES);
   }
   grid_dep_wait();
   grid_dep_launch();
@@ -220,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   if (tid == 0) {
     for (int i = 0; i < PS; ++i) {
       mbar_init(pfull + 8 * i, 1);
-      mbar_init(pempty + 8 * i, 8 * 32);
+      mbar_init(pempty + 8 * i, kDecWarps * 32);
     }
     for (int i = 0; i < AS; ++i) {
       mbar_init(afull + 8 * i, 8 * 32);
@@ -236,7 +257,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     }
     *abort_word = 0u;
     fence_mbar_init();
-    prefetch_tmap(&p.wmap);
     prefetch_tmap(&p.xmap);
   }
   if (warp == kMmaWarp) {
@@ -252,17 +272,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
 
   if (warp == kWProdWarp) {
     // ---------------- weight producer ----------------
-    if (lane == 0) {
-      for (int j = 0; j < nit; ++j) {
-        const int u = u0 + j;
-        const int tile = u / C, chunk = u - tile * C;
-        const int ps = j % PS;
-        if (j >= PS && !mbar_wait(pempty + 8 * ps, ((j / PS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
-        mbar_arrive_expect_tx(pfull + 8 * ps, kPackedStage);
-        tma_load_3d(base + CF::kPacked + ps * kPackedStage, &p.wmap, 0, chunk, (tile % p.R8) * 8, pfull + 8 * ps);
+    // Stage uses walk the range as groups of up to KC consecutive items of one segment; lanes 0-7 each copy their
+    // row tile's KC units (contiguous in the row-tile-major layout) with one bulk copy.  (One 3-D tensor copy of
+    // the 8 units of an item per stage measured ~0.45 us per issue on B200, a limit of ~27 GB/s per SM.)
+    const uint64_t pol = policy_evict_first();
+    int use = 0;
+    bool ok = true;
+    for (int s = 0; s < nseg && ok; ++s) {
+      const Seg sg = seg_of(tile_first + s, u0, u1, C);
+      const int rb = sg.tile % p.R8, nr = min(8, p.Rout - rb * 8);
+      for (int c0 = sg.cb; c0 < sg.ce; c0 += KC, ++use) {
+        const int n = min(KC, sg.ce - c0), ps = use % PS;
+        if (use >= PS && !mbar_wait(pempty + 8 * ps, ((use / PS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(pfull + 8 * ps, (uint32_t)(nr * n * MBP_C12_UNIT_BYTES));
+        __syncwarp();
+        if (lane < nr)
+          bulk_g2s_hint(base + CF::kPacked + ps * kPackedStage + lane * KC * MBP_C12_UNIT_BYTES,
+                        p.units + ((size_t)(rb * 8 + lane) * C + c0) * MBP_C12_UNIT_BYTES,
+                        (uint32_t)n * MBP_C12_UNIT_BYTES, pfull + 8 * ps, pol);
       }
     }
-    __syncwarp();  // lanes 1-31 wait here for the producing lane
+    __syncwarp();
   } else if (warp == kXWarp) {
     // ---------------- x producer ----------------
     if (lane == 0) {
@@ -278,8 +311,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     __syncwarp();
   } else if (warp == kSchedWarp) {
     // ---------------- MMA scheduler ----------------
-    // Waits for item j's A and x stages (and, when j starts segment s >= 2, for the epilogue to have released
-    // segment s-2's accumulator) while the issuer is still feeding item j-1 to the tensor pipe, then meets it on a
+    // Waits for item j's A and x stages (and, when j starts segment s >= NACC, for the epilogue to have released
+    // segment s-NACC's accumulator) while the issuer is still feeding item j-1 to the tensor pipe, then meets it on a
     // named barrier.  Every round is always met, so a timed-out wait ends both warps' loops through the abort word
     // instead of a missing partner.
     bool ok = true;
@@ -292,8 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         seg_end += C;
       }
       if (lane == 0 && ok) {
-        if (s >= 2 && u % C == 0)
-          ok = mbar_wait(accempty + 8 * (s & 1), ((s >> 1) - 1) & 1, MBP_DEV_TIMEOUT_MMA, p.wait_ns);
+        if (s >= NACC && u % C == 0)  // segment s reuses accumulator s % NACC: wait for segment s - NACC's epilogue
+          ok = mbar_wait(accempty + 8 * (s % NACC), ((s / NACC) - 1) & 1, MBP_DEV_TIMEOUT_MMA, p.wait_ns);
         ok = ok && mbar_wait(afull + 8 * (j % AS), (j / AS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns) &&
              mbar_wait(xfull + 8 * (j % XS), (j / XS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns);
         if (!ok) *abort_word = 1u;
@@ -320,23 +353,32 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         const int as = j % AS, xs = j % XS;
         tc_fence_after();
         const uint64_t da = da0 + (uint64_t)((as * kAStage) >> 4), db = db0 + (uint64_t)((xs * CF::kXStage) >> 4);
-        const uint32_t d = tmem + (uint32_t)(s & 1) * acc_cols;
+        const uint32_t d = tmem + (uint32_t)(s % NACC) * acc_cols;
+        if constexpr (CF::kTA) {
+          const uint32_t ta = tmem + a_col0 + (uint32_t)as * 32u;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) tc_mma(d, da + 2 * k, db + 2 * k, idesc, (u != seg_beg || k != 0) ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) tc_mma_ts(d, ta + 8 * k, db + 2 * k, idesc, (u != seg_beg || k != 0) ? 1u : 0u);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) tc_mma(d, da + 2 * k, db + 2 * k, idesc, (u != seg_beg || k != 0) ? 1u : 0u);
+        }
         tc_commit(aempty + 8 * as);
         tc_commit(xempty + 8 * xs);
         // the segment's last item: the accumulator is complete once these MMAs are
-        if (u + 1 == seg_end || u + 1 == u1) tc_commit(accfull + 8 * (s & 1));
+        if (u + 1 == seg_end || u + 1 == u1) tc_commit(accfull + 8 * (s % NACC));
       }
       __syncwarp();
     }
   } else if (warp < kXWarp) {
     // ---------------- decoders: group gi takes items gi, gi + kGroups, ... ----------------
-    const int dw = warp - kDec0, gi = dw >> 3, d = dw & 7;
+    // Row tile d of the 128-row tile.  With A in TMEM a warp may only write its lane quadrant (warp % 4), so row tile
+    // d (lanes 16d .. 16d+15) goes to a warp of quadrant d / 2: the warps of a group cover quadrants 2, 3, 0, 1 twice.
+    const int dw = warp - kDec0, gi = dw >> 3, di = dw & 7;
+    const int d = CF::kTA ? 2 * ((di + kDec0) & 3) + (di >> 2) : di;
     const uint32_t xr = base + CF::kMask + dw * kMaskUnitBytes;
     mask_clear(xr, kMaskUnitBytes, lane);
     const int g = lane >> 2, t = lane & 3;
-    // destination rows r = 16 d + 8 rh + g inside the 128-row A tile (SW128 K-major)
+    // shared-memory A: destination rows r = 16 d + 8 rh + g inside the 128-row A tile (SW128 K-major)
     uint32_t dst[2][2];
 #pragma unroll
     for (int rh = 0; rh < 2; ++rh) {
@@ -345,58 +387,76 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       dst[rh][0] = row + ((uint32_t)((2 * t) ^ (r & 7)) << 4);
       dst[rh][1] = row + ((uint32_t)((2 * t + 1) ^ (r & 7)) << 4);
     }
-    int cur_tile = -1;
-    bool valid = false;
+    // Every decoder warp waits on and releases every stage use; in a use of n items starting at item j0, group gi
+    // decodes the items j with j % kGroups == gi.
+    bool valid = false, ok = true;
     uint32_t T0 = 0, T1 = 0;
     EscCursor cur;
-    for (int j = gi; j < nit; j += kGroups) {
-      const int u = u0 + j;
-      const int tile = u / C, chunk = u - tile * C;
-      if (tile != cur_tile) {  // a new segment: this warp's row tile, its table and its escape slice
-        cur_tile = tile;
-        const Seg sg = seg_of(tile, u0, u1, C);
-        const int rt = (tile % p.R8) * 8 + d;
-        valid = rt < p.Rout;
-        T0 = T1 = 0;
-        if (valid) {
-          const uint32_t b = p.bases[rt];
-          T0 = table_lo(b);
-          T1 = table_hi(b);
-          cur.init(p.esc, p.esc_off[(size_t)rt * C + sg.cb], p.esc_off[(size_t)rt * C + sg.ce], lane);
-        } else {
-          cur.init(p.esc, 0, 0, lane);
-        }
-      }
-      const int ps = j % PS, as = j % AS;
-      if (!mbar_wait(pfull + 8 * ps, (j / PS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns)) break;
-      const unsigned char* un = sm + CF::kPacked + ps * kPackedStage + d * MBP_C12_UNIT_BYTES + lane * 16;
-      const uint4 p0 = *reinterpret_cast<const uint4*>(un);
-      const uint4 p1 = *reinterpret_cast<const uint4*>(un + 512);
-      const uint4 p2 = *reinterpret_cast<const uint4*>(un + 1024);
-      uint32_t A[16];
-      const uint32_t c = (uint32_t)chunk;
-      if (valid) cur.seek(c, lane);
-      if (valid && cur.next_chunk == c) {
-        uint32_t tgt[1] = {0u};
-        cur.scatter<1>(c, c + 1, xr, kMaskUnitBytes, lane, tgt);
-        __syncwarp();
-        uint4 m0, m1;
-        take_mask(xr, tgt[0], lane, m0, m1);
-        decode_unit_m(p0, p1, p2, T0, T1, m0, m1, A);
+    int use = 0, j0 = 0;
+    for (int s = 0; s < nseg && ok; ++s) {
+      const Seg sg = seg_of(tile_first + s, u0, u1, C);
+      // a new segment: this warp's row tile, its table and its escape slice
+      const int rt = (sg.tile % p.R8) * 8 + d;
+      valid = rt < p.Rout;
+      T0 = T1 = 0;
+      if (valid) {
+        const uint32_t b = p.bases[rt];
+        T0 = table_lo(b);
+        T1 = table_hi(b);
+        cur.init(p.esc, p.esc_off[(size_t)rt * C + sg.cb], p.esc_off[(size_t)rt * C + sg.ce], lane);
       } else {
-        decode_unit(p0, p1, p2, T0, T1, A);
+        cur.init(p.esc, 0, 0, lane);
       }
-      // A[0] depends on p0 and p2, A[8] on p1: all three loads have returned before the stage is handed back
-      mbar_arrive_dep(pempty + 8 * ps, A[0] ^ A[8]);
-      if (j >= AS && !mbar_wait(aempty + 8 * as, ((j / AS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
-      unsigned char* a = sm + CF::kA + as * kAStage;
+      for (int c0 = sg.cb; c0 < sg.ce && ok; c0 += KC, ++use) {
+        const int n = min(KC, sg.ce - c0), ps = use % PS;
+        if (!mbar_wait(pfull + 8 * ps, (use / PS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns)) {
+          ok = false;
+          break;
+        }
+        uint32_t dep = 0;
+        for (int jj = (gi - j0 % kGroups + kGroups) % kGroups; jj < n; jj += kGroups) {
+          const int j = j0 + jj, as = j % AS;
+          const unsigned char* un =
+              sm + CF::kPacked + ps * kPackedStage + (d * KC + jj) * MBP_C12_UNIT_BYTES + lane * 16;
+          const uint4 p0 = *reinterpret_cast<const uint4*>(un);
+          const uint4 p1 = *reinterpret_cast<const uint4*>(un + 512);
+          const uint4 p2 = *reinterpret_cast<const uint4*>(un + 1024);
+          uint32_t A[16];
+          const uint32_t c = (uint32_t)(c0 + jj);
+          if (valid) cur.seek(c, lane);
+          if (valid && cur.next_chunk == c) {
+            uint32_t tgt[1] = {0u};
+            cur.scatter<1>(c, c + 1, xr, kMaskUnitBytes, lane, tgt);
+            __syncwarp();
+            uint4 m0, m1;
+            take_mask(xr, tgt[0], lane, m0, m1);
+            decode_unit_m(p0, p1, p2, T0, T1, m0, m1, A);
+          } else {
+            decode_unit(p0, p1, p2, T0, T1, A);
+          }
+          dep ^= A[0] ^ A[8];  // A[0] depends on p0 and p2, A[8] on p1
+          if (j >= AS && !mbar_wait(aempty + 8 * as, ((j / AS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) {
+            ok = false;
+            break;
+          }
+          if constexpr (CF::kTA) {
+            tc_st_a(tmem + ((uint32_t)(16 * d) << 16) + a_col0 + (uint32_t)as * 32u, A);
+            tc_fence_before();  // the stores are complete (wait::st) and ordered before the arrive
+          } else {
+            unsigned char* a = sm + CF::kA + as * kAStage;
 #pragma unroll
-      for (int rh = 0; rh < 2; ++rh) {
-        *reinterpret_cast<uint4*>(a + dst[rh][0]) = make_uint4(A[0 + rh], A[2 + rh], A[4 + rh], A[6 + rh]);
-        *reinterpret_cast<uint4*>(a + dst[rh][1]) = make_uint4(A[8 + rh], A[10 + rh], A[12 + rh], A[14 + rh]);
+            for (int rh = 0; rh < 2; ++rh) {
+              *reinterpret_cast<uint4*>(a + dst[rh][0]) = make_uint4(A[0 + rh], A[2 + rh], A[4 + rh], A[6 + rh]);
+              *reinterpret_cast<uint4*>(a + dst[rh][1]) = make_uint4(A[8 + rh], A[10 + rh], A[12 + rh], A[14 + rh]);
+            }
+            fence_async_smem();
+          }
+          mbar_arrive(afull + 8 * as);
+        }
+        // this warp's loads from the stage have returned (dep) before the stage goes back to the producer
+        mbar_arrive_dep(pempty + 8 * ps, dep);
+        j0 += n;
       }
-      fence_async_smem();
-      mbar_arrive(afull + 8 * as);
     }
   } else {
     // ---------------- epilogue: TMEM -> registers -> the output, or a partial tile ----------------
@@ -408,8 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       const Seg sg = seg_of(tile_first + s, u0, u1, C);
       const int rb = sg.tile % p.R8, tok0 = (sg.tile / p.R8) * p.bn;
       const int row = rb * 128 + row_l;
-      const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s & 1) * acc_cols;
-      bool ok = mbar_wait(accfull + 8 * (s & 1), (s >> 1) & 1, MBP_DEV_TIMEOUT_MMA, p.wait_ns);
+      const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s % NACC) * acc_cols;
+      bool ok = mbar_wait(accfull + 8 * (s % NACC), (s / NACC) & 1, MBP_DEV_TIMEOUT_MMA, p.wait_ns);
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
       tc_fence_after();
       if (sg.cb == 0 && sg.ce == C) {
@@ -427,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(accempty + 8 * (s & 1));
+        if (lane == 0) mbar_arrive(accempty + 8 * (s % NACC));
         continue;
       }
       // part of a split tile: the FP32 partial to this CTA's slot (column-major: element (r, col) at col*128 + r)
@@ -441,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(accempty + 8 * (s & 1));  // the next segment may reuse this accumulator
+      if (lane == 0) mbar_arrive(accempty + 8 * (s % NACC));  // a later segment may reuse this accumulator
       // ticket: the contributor that arrives last adds every part, in CTA order
       __threadfence();
       named_bar_sync(kEpiBar, 128);
@@ -527,19 +587,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   }
 }
 
-// units [R][C][1536 bytes] viewed as a 3-D tensor of u64: {192, C, R}, box {192, 1, 8}
-bool encode_units_3d(CUtensorMap* map, const void* units, int R, int C) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[3] = {192, (cuuint64_t)C, (cuuint64_t)R};
-  const cuuint64_t strides[2] = {(cuuint64_t)MBP_C12_UNIT_BYTES, (cuuint64_t)C * MBP_C12_UNIT_BYTES};
-  const cuuint32_t box[3] = {192, 1, 8};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(units), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 using KernelFn = void (*)(GemmParams);
 
 template <class CF>
@@ -547,33 +594,38 @@ KernelFn kernel_of() {
   return reinterpret_cast<KernelFn>(&k_gemm<CF>);
 }
 
+struct Inst {
+  KernelFn fn;
+  int smem;
+  int nacc, tmem_a;  // accumulators; TMEM columns of the A ring (0: A in shared memory)
+};
+
 template <class CF>
-KernelFn inst(int* smem) {
-  *smem = CF::kSmem;
-  return kernel_of<CF>();
+Inst inst() {
+  return Inst{kernel_of<CF>(), CF::kSmem, CF::kNAcc, CF::kTA ? CF::kAS * 32 : 0};
 }
 
-// The instance for a token tile of bn tokens (bn % 16 == 0, <= 256) and its shared-memory request.
+// The instance for a token tile of bn tokens (bn % 16 == 0, <= 256).
 // MBP_GEMM_CFG=<i> selects the i-th instance of the class (ring-depth sweeps).
-KernelFn pick(int bn, int* smem) {
+Inst pick(int bn) {
   static const int sel = getenv("MBP_GEMM_CFG") ? atoi(getenv("MBP_GEMM_CFG")) : -1;
   if (bn <= 32) {
     switch (sel) {
-      case 0: return inst<CfgS0>(smem);
-      case 2: return inst<CfgS2>(smem);
-      default: return inst<CfgS1>(smem);
+      case 0: return inst<CfgS0>();
+      case 2: return inst<CfgS2>();
+      default: return inst<CfgS1>();
     }
   }
   if (bn <= 128) {
     switch (sel) {
-      case 0: return inst<CfgM0>(smem);
-      default: return inst<CfgM1>(smem);
+      case 0: return inst<CfgM0>();
+      default: return inst<CfgM1>();
     }
   }
   switch (sel) {
-    case 0: return inst<CfgL0>(smem);
-    case 2: return inst<CfgL2>(smem);
-    default: return inst<CfgL1>(smem);
+    case 0: return inst<CfgL0>();
+    case 2: return inst<CfgL2>();
+    default: return inst<CfgL1>();
   }
 }
 
@@ -602,7 +654,7 @@ int sm_count() {
 
 // The decomposition of a call: token tile width, tiles, items and the grid.
 struct Plan {
-  int bn, R8, tiles, G, tcols;
+  int bn, R8, tiles, G, acc_cols;
   long long U;
 };
 
@@ -627,10 +679,7 @@ Plan make_plan(int n_out, int k, int m, int sms, bool streamk) {
     if (G < 1) G = 1;
   }
   pl.G = (int)G;
-  const int acc = pl.bn <= 32 ? 32 : ((pl.bn + 31) / 32) * 32;  // accumulator columns (a tcgen05.ld reads 32)
-  int cols = 32;
-  while (cols < 2 * acc) cols *= 2;
-  pl.tcols = cols;
+  pl.acc_cols = pl.bn <= 32 ? 32 : ((pl.bn + 31) / 32) * 32;  // accumulator columns
   return pl;
 }
 
@@ -659,15 +708,14 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   if (pl.U > 0x7fffffffLL / 2) return MBP_ERR_SHAPE;  // items are indexed with 32-bit integers
   // no (or a too small) workspace, or more tiles than tickets: whole tiles per CTA
   if (!ws || ws_bytes < ws_bytes_for(pl) || pl.tiles > kMaxTickets) pl = make_plan(n_out, w->k, m, sms, false);
-  int smem = 0;
-  const KernelFn fn = pick(pl.bn, &smem);
-  int rc = ensure_attr(fn, smem);
+  const Inst in = pick(pl.bn);
+  int tcols = 32;  // TMEM: the accumulators, then the A ring of a TMEM-resident instance
+  while (tcols < in.nacc * pl.acc_cols + in.tmem_a) tcols *= 2;
+  if (tcols > 512) return MBP_ERR_SMEM;
+  int rc = ensure_attr(in.fn, in.smem);
   if (rc) return rc;
   GemmParams p;
-  const int R = w->n / 16, C = w->k / 64;
-  const TmapKey wkey{w->units, (uint64_t)R, (uint64_t)C, 0, 0, 0, 0x200u};
-  if (!cached_map(&p.wmap, wkey, [&](CUtensorMap* mp) { return encode_units_3d(mp, w->units, R, C); }))
-    return MBP_ERR_TMAP;
+  const int C = w->k / 64;
   if (!encode_bf16_2d_cached(&p.xmap, x, (uint64_t)m, (uint64_t)w->k, (uint64_t)w->k, (uint32_t)pl.bn, 64u,
                              CU_TENSOR_MAP_SWIZZLE_128B))
     return MBP_ERR_TMAP;
@@ -688,12 +736,13 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   p.bn = pl.bn;
   p.f32out = f32 ? 1 : 0;
   p.vec_out = ((uintptr_t)out & 15u) == 0 && ldo % 8 == 0;
-  p.tcols = pl.tcols;
+  p.tcols = tcols;
+  p.acc_cols = pl.acc_cols;
   p.wait_ns = wait_limit_ns();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.G);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = in.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   int na = 0;
@@ -705,7 +754,7 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, fn, p) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+  return cudaLaunchKernelEx(&cfg, in.fn, p) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
 }
 
 }  // namespace
