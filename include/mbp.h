@@ -143,22 +143,16 @@ int mbp_gemv_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t
 int mbp_gemv_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
                      const mbp_gemv_geom* geom, cudaStream_t stream);
 
-/* ---- tcgen05 tensor-core path, weights unpacked in shared memory (replaces the dense BF16 verify GEMMs
- * ss_gemm S:783, q_kernel S:979 / qb_kernel S:4576, ol_projection S:1547, projection S:2985, the register-A
- * wgmma family for 16-32 tokens m32w_gemm S:2395, and the out-of-scope cuBLASLt routes S:2309-2376):
- * out[m, n_out] = x . W[0:n_out]^T, FP32 accumulation in TMEM, any m >= 1 (token tiles of up to 256).
- * The work is split evenly over the SMs (stream-K): parts of split tiles go through `workspace` as FP32 partial
- * tiles and the last contributor of a tile adds them in a fixed order (results do not depend on timing).
- * workspace: mbp_gemm_workspace(n_out, k, m) bytes, 256-byte aligned, ZERO-FILLED before its first use: its first
- * 64 KiB hold one ticket per tile, which every call leaves at zero again, so one workspace serves calls of any
- * shape (the largest size they need); calls that share a workspace must be ordered on one stream.  NULL (or too
- * small) runs one whole tile per CTA instead, which leaves SMs idle when the tile count is not a multiple of the
- * SM count. ---- */
-size_t mbp_gemm_workspace(int n_out, int k, int m);
-int mbp_gemm_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo, void* workspace,
-                 size_t workspace_bytes, cudaStream_t stream);
-int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo, void* workspace,
-                     size_t workspace_bytes, cudaStream_t stream);
+/* ---- verify-path GEMM on the tcgen05 tensor cores (replaces the dense BF16 verify GEMMs ss_gemm S:783,
+ * q_kernel S:979 / qb_kernel S:4576, ol_projection S:1547, projection S:2985, and the out-of-scope cuBLASLt routes
+ * S:2309-2376): out[m, n_out] = x . W[0:n_out]^T, FP32 accumulation in TMEM, any m >= 1 (tiles of up to 256
+ * tokens; intended for m > 32).  The weights stay packed in HBM; decoded tiles go to TMEM as the MMA's A
+ * operand.  Short-K shapes split the tokens into tiles, few-tile shapes split K over a thread-block cluster
+ * (reduced in distributed shared memory, a fixed order: repeated calls give identical bits). ---- */
+int mbp_gemm_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo,
+                 cudaStream_t stream);
+int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
+                     cudaStream_t stream);
 
 /* ---- tensor-parallel helpers (no counterpart in the reference, which is single-GPU) ----
  * Column-parallel: each rank computes a [m, ns] shard of out; an all-gather into one buffer yields [P][m][ns];

@@ -274,8 +274,10 @@ MBP_DEV uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return d;
 }
 
-// 8 values of one k-step: low bytes in L0 (values 0-3) and L1 (values 4-7), code word C.
-// T0/T1 = byte table base..base+7 (the high byte, without sign, of each exponent offset).
+// Decodes the 8 weights of one k-step.  L0 / L1 carry the low bytes of weights 0-3 / 4-7 and C their code
+// word.  The 3-bit exponent offsets of C, masked to nibbles, select through prmt a byte of the 8-entry table T0:T1
+// (exponent bytes base .. base+7); a second prmt interleaves those high bytes with the low bytes into bf16 pairs
+// in the A-fragment order, and the sign bits are moved from their code-word positions to bit 15 of each half.
 MBP_DEV void decode8(uint32_t L0, uint32_t L1, uint32_t C, uint32_t T0, uint32_t T1, uint32_t* a) {
   const uint32_t cm = C & 0x77777777u;
   const uint32_t h0 = prmt(T0, T1, cm);

@@ -1,38 +1,27 @@
-// Tensor-core path: out[m, n] = x[m, k] . W[n, k]^T on the 5th-generation tensor cores (tcgen05 + TMEM), the
-// weights unpacked from the 12-bit format in shared memory.  Used for the verify shapes (M > 32) and for the
-// decode shapes whose token count makes the register-decode GEMV latency-bound.
+// Verify-path GEMM for larger token counts (M > 32): out[m, n] = x[m, k] . W[n, k]^T on the 5th-generation
+// tensor cores (tcgen05 + TMEM), weights unpacked from the 12-bit format in shared memory.
 //
 // Replaces the reference's dense BF16 verify GEMMs (submission.py: ss_gemm S:783<17-123>, q_kernel
-// S:979<25-170>, qb_kernel S:4576, ol_projection S:1547<18-106>, projection S:2985), its register-A wgmma
-// family for 16-32 tokens (m32w_gemm S:2395) and its cuBLASLt routes (S:2309-2376, out of scope); here the
-// weights stay packed in HBM.
+// S:979<25-170>, qb_kernel S:4576, ol_projection S:1547<18-106>, projection S:2985) and its cuBLASLt routes
+// (S:2309-2376, out of scope), which read unpacked BF16 weights; here the weights stay packed in HBM.
 //
-// Work decomposition (stream-K): a TILE is 128 weight rows (8 row tiles) x BN tokens; an ITEM is one 64-column
-// chunk of a tile.  The items, tile-major, are cut into gridDim.x equal contiguous ranges, one per CTA (one CTA
-// per SM), so every SM streams the same number of packed bytes whatever the tile count (the fused QKV+gate
-// matrix has 112 tiles for 148 SMs).  A CTA walks its range as SEGMENTS (its part of one tile).  A segment that
-// covers the whole tile is stored directly; the parts of a split tile are written as FP32 partial tiles to the
-// caller's workspace, and the contributor that finishes last (an atomic ticket per tile) adds all parts in CTA
-// order -- a fixed order, so the result does not depend on timing -- and stores the tile.  No CTA waits for
-// another.  Without a workspace every CTA takes one whole tile.
-//
-// Warp roles (24 warps):
-//   warp 0       producer of the weights: a stage holds KC consecutive items, lanes 0-7 each fill their row
-//                tile's KC packed units (contiguous) with one TMA bulk copy, PS stages deep;
-//   warp 18      TMA producer of x: one 2-D box (BN rows x 128 bytes, 128-byte swizzle) per item;
-//   warp 19      MMA scheduler: waits for an item's decoded-A and x stages (and, at a segment start, for the
-//                epilogue to release the accumulator) and hands the item to the issuer on a named barrier;
-//   warp 1       allocates TMEM (accumulators, and the decoded-A ring); lane 0 issues tcgen05.mma (M=128, N=BN,
-//                K=16) x4 per item and commits the stages back to their producers and finished segments to the
-//                epilogue;
-//   warps 2-17   decoders in two groups of 8 warps taking alternate items; each warp decodes one row tile (12-bit
-//                decode and escape restoration in registers, as in the GEMV) and writes it as the MMA's A operand:
-//                into TMEM with tcgen05.st (the instances used; A then never touches shared memory, whose
-//                bandwidth otherwise bounds the 256-token tiles), or into the canonical SW128 K-major layout of a
-//                shared-memory A stage;
-//   warps 20-23  epilogue: warp 20+q reads TMEM lanes 32q..32q+31 (tcgen05.ld 32x32b), stores the tile or its
-//                partial and releases the accumulator, while the next segment's MMAs run in the other one.
-// All waits are bounded (status word, no trap); TMEM is always released.
+// CTA tile: 128 weight rows (8 row tiles) x BN tokens (<= 256) x a K range; `split` CTAs of a cluster share
+// one tile's K range and reduce through distributed shared memory.  Warp roles:
+//   warp 0       TMA producer of the weights: per 64-column chunk, one 3-D box of 8 packed units (12 KB);
+//   warp 18      TMA producer of x: per chunk one 2-D box of the x tile (BN rows x 128 bytes, 128-byte
+//                swizzle); the two rings run independently, so an x stage is refilled as soon as its MMA is done;
+//   warp 19      MMA scheduler: waits for each chunk's A and x stages and hands the chunk to the issuer on a
+//                named barrier, so the issuing thread never polls an mbarrier behind its own MMAs;
+//   warp 1       allocates TMEM (the accumulator, then the decoded-A ring); lane 0 issues tcgen05.mma (M=128,
+//                N=BN, K=16, BF16 -> FP32) x4 per chunk, A from TMEM and B = x from a K-major SW128 shared-memory
+//                descriptor; tcgen05.commit frees the A and x stages and finally signals the accumulator;
+//   warps 2-17   decoders in kGroups groups of 8 warps; group g handles every kGroups-th chunk, each warp decodes
+//                one row tile in registers (same decode and escape cursor as the GEMV), transposes its K pairs
+//                across its lane quads and writes the tile with tcgen05.st straight into TMEM as the MMA's A
+//                operand: the decoded weights never pass through shared memory, whose bandwidth (TMA writes and
+//                the MMA's operand reads) otherwise bounds the 256-token tiles.  Afterwards they read the
+//                accumulator (tcgen05.ld 32x32b) and store (or cluster-reduce) it.
+// All waits are bounded; TMEM is always released.
 #include "common.cuh"
 #include "escape.cuh"
 #include "tmap.h"
@@ -46,79 +35,74 @@ using namespace mbp;
 
 namespace {
 
-constexpr int kGroups = 2;                 // decoder groups working on alternate items
+constexpr int kGroups = 2;                 // decoder groups working on alternate chunks
 constexpr int kDecWarps = 8 * kGroups;
-constexpr int kWProdWarp = 0;
-constexpr int kMmaWarp = 1;
-constexpr int kDec0 = 2;
-constexpr int kXWarp = kDec0 + kDecWarps;  // 18
-constexpr int kSchedWarp = kXWarp + 1;     // 19
-constexpr int kEpi0 = kSchedWarp + 1;      // 20 (a multiple of 4: warp kEpi0 + q owns TMEM lane quadrant q)
-constexpr int kThreads = 32 * (kEpi0 + 4);
-constexpr int kHandBar = 1;                // named barrier: scheduler -> issuer hand-over (64 threads)
-constexpr int kEpiBar = 2;                 // named barrier of the 4 epilogue warps (128 threads)
-constexpr int kAStage = 128 * 128;                    // 128 rows x 64 bf16
+constexpr int kXWarp = 2 + kDecWarps;      // the x producer
+constexpr int kSchedWarp = 3 + kDecWarps;  // waits for each chunk's operands on behalf of the MMA issuer
+constexpr int kThreads = 32 * (4 + kDecWarps);
+constexpr int kHandBar = 1;                // named barrier of the scheduler -> issuer hand-over (64 threads)
+constexpr int kPS = 6;                     // packed ring depth
+constexpr int kAS = 2;                     // decoded-A ring depth
+constexpr int kXS = 4;                     // x ring depth
+// Decoder group g owns chunks i = g (mod kGroups).  A ring whose barriers the decoders wait on must give every
+// stage to a single group (depth a multiple of kGroups): otherwise a group could wait for use k+1 of a stage
+// while use k, owned by the other group and completed out of order by the TMA engine, is still pending, and
+// mbarrier parity waits, which only tell the current phase from the previous one, would return on the stale
+// phase (wrong data, and arrivals counted into the wrong phase).
+static_assert(kPS % kGroups == 0 && kAS % kGroups == 0, "ring depths must be multiples of the decoder groups");
+constexpr int kPackedStage = 8 * MBP_C12_UNIT_BYTES;  // 12 KB
 constexpr int kMaxSmem = 227 * 1024;
-constexpr int kMaxParts = 8;               // contributors of one split tile (the host's plan keeps to it)
-static_assert(kEpi0 % 4 == 0, "epilogue warp kEpi0 + q must own TMEM lane quadrant q");
 
 struct __align__(64) GemmParams {
-  CUtensorMap xmap;  // x [m, k] bf16, box {64 columns, bn rows}, 128-byte swizzle
+  CUtensorMap wmap;  // units as [R][C][192 x u64], box {192, 1, 8}
+  CUtensorMap xmap;  // x [m, k] bf16, box {64 columns, BN rows}, 128-byte swizzle
   const uint8_t* units;
   const uint8_t* bases;
   const int32_t* esc_off;
   const uint32_t* esc;
   void* out;
-  float* ws_part;  // [2 * gridDim.x][bn][128] FP32 partial tiles (slot 2c: CTA c's first segment, 2c+1: its last)
-  int* ws_cnt;     // [tiles] contributor tickets, zero between calls
-  long long U;     // items = tiles * C
-  int C, Rout, R8, m, ldo, bn, f32out;
-  int vec_out;     // out and ldo allow 4-row vector stores (16-byte aligned base, ldo % 8 == 0)
-  int tcols;       // TMEM columns allocated
-  int acc_cols;    // columns of one accumulator (>= bn, a multiple of 32)
+  int C, Rout, m, ldo, bn, split;
+  int f32out;
   unsigned long long wait_ns;  // limit of every bounded wait
+  int direct;                  // the issuer polls the stage barriers itself (no scheduler hand-over)
 };
 
-// Layout of one instance: PS weight stages of KC items each (8 row tiles x KC consecutive packed units, filled
-// by one bulk copy of KC units per row tile), AS decoded-A stages (TA: in TMEM, 32 columns each after the
-// accumulators; else in shared memory), XS x stages of up to BNMAX tokens, NACC TMEM accumulators (2 lets a
-// segment's epilogue overlap the next segment's MMAs).
-template <int PS, int KC, int AS, int XS, int BNMAX, bool TA, int NACC>
-struct Cfg {
-  static constexpr int kPS = PS, kKC = KC, kAS = AS, kXS = XS, kBNMax = BNMAX, kNAcc = NACC;
-  static constexpr bool kTA = TA;
-  static constexpr int kPackedStage = 8 * KC * MBP_C12_UNIT_BYTES;
-  static constexpr int kXStage = BNMAX * 128;
-  static constexpr int kPacked = 0;
-  static constexpr int kA = kPacked + PS * kPackedStage;  // multiples of 1024 (SW128 atoms)
-  static constexpr int kX = kA + (TA ? 0 : AS * kAStage);
-  static constexpr int kMask = kX + XS * kXStage;
-  static constexpr int kBars = kMask + kDecWarps * kMaskUnitBytes;
-  // pfull/pempty[PS], afull/aempty[AS], xfull/xempty[XS], accfull/accempty[2]
-  static constexpr int kMisc = kBars + 8 * (2 * PS + 2 * AS + 2 * XS + 4);
-  static constexpr int kTotal = kMisc + 16;    // TMEM base, abort word, ticket
-  static constexpr int kSmem = kTotal + 1024;  // + alignment slack
-  // Stage ownership: decoder group g takes items g (mod kGroups).  A ring whose barriers only one group waits on
-  // per use must give every stage to a single group (depth a multiple of kGroups): otherwise a group could wait for
-  // use k+1 of a stage while use k, owned by the other group and completed out of order by the TMA engine, is
-  // still pending, and mbarrier parity waits, which only tell the current phase from the previous one, would
-  // return on the stale phase.  The decoded-A ring is such a ring; every decoder warp waits on and releases every
-  // use of a weight stage, so that ring may have any depth.
-  static_assert(AS % kGroups == 0, "the decoded-A ring depth must be a multiple of the decoder groups");
-  static_assert(kSmem <= kMaxSmem, "shared memory");
+// Non-blocking probe of an mbarrier phase.
+MBP_DEV bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+struct GLayout {
+  int packed, a, x, xr, bars, tmem_slot, total;
 };
 
-// Instances (ring depths per token-tile class); pick() chooses one per call.
-using CfgS0 = Cfg<3, 4, 2, 4, 32, false, 2>;
-using CfgS1 = Cfg<3, 4, 4, 4, 32, true, 2>;
-using CfgS2 = Cfg<4, 4, 8, 4, 32, true, 2>;
-using CfgM0 = Cfg<2, 4, 2, 4, 128, false, 2>;
-using CfgM1 = Cfg<3, 4, 4, 4, 128, true, 2>;
-using CfgL0 = Cfg<3, 2, 2, 3, 256, false, 2>;
-using CfgL1 = Cfg<2, 4, 4, 3, 256, true, 1>;
-using CfgL2 = Cfg<3, 2, 8, 3, 256, true, 1>;
+__host__ __device__ inline GLayout gemm_layout(int bn) {
+  GLayout L;
+  L.packed = 0;
+  L.a = L.packed + kPS * kPackedStage;  // (no shared-memory A: the decoded tiles live in TMEM)
+  L.x = L.a;                            // multiple of 1024
+  L.xr = L.x + kXS * bn * 128;          // bn multiple of 16 -> multiple of 2048
+  L.bars = L.xr + kDecWarps * kMaskUnitBytes;
+  L.tmem_slot = L.bars + 8 * (2 * kPS + 2 * kAS + 2 * kXS + 1);
+  L.total = L.tmem_slot + 16;
+  return L;
+}
 
-MBP_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+MBP_DEV void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
 MBP_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 MBP_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -133,14 +117,6 @@ MBP_DEV uint32_t idesc_bf16(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-MBP_DEV void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc)
-      : "memory");
-}
-
 // A from TMEM (M=128 lanes = rows, 8 columns per K=16: a column holds two consecutive K elements, low half first).
 MBP_DEV void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
@@ -150,11 +126,53 @@ MBP_DEV void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t id
       : "memory");
 }
 
-// 16 lanes x 32 columns from the mma.sync A-fragment registers of a decoded unit: in the .16x128b shape thread
-// 4g + t holds (lane g, column t) and (lane g + 8, column t) of each 4-column block, and .x8 repeats the block
-// along the columns with the next register pair -- A[4q], A[4q+1] (k pairs t of step q) then A[4q+2], A[4q+3]
-// (k pairs t + 4) -- so the sixteen registers land as 16 rows x 64 K in order.
-MBP_DEV void tc_st_a(uint32_t taddr, const uint32_t (&a)[16]) {
+// 4 x 4 transpose across the 4 lanes of a quad (t = lane & 3): afterwards lane t holds, at index a, what lane a
+// held at index t.  Two butterfly stages (partners t ^ 2, then t ^ 1), each exchanging the two elements whose
+// index differs from t in that stage's bit.
+MBP_DEV void quad_transpose(uint32_t& m0, uint32_t& m1, uint32_t& m2, uint32_t& m3, int t) {
+  const bool b1 = (t & 2) != 0, b0 = (t & 1) != 0;
+  uint32_t s0 = b1 ? m0 : m2, s1 = b1 ? m1 : m3;
+  s0 = __shfl_xor_sync(0xffffffffu, s0, 2);
+  s1 = __shfl_xor_sync(0xffffffffu, s1, 2);
+  if (b1) {
+    m0 = s0;
+    m1 = s1;
+  } else {
+    m2 = s0;
+    m3 = s1;
+  }
+  s0 = b0 ? m0 : m1;
+  s1 = b0 ? m2 : m3;
+  s0 = __shfl_xor_sync(0xffffffffu, s0, 1);
+  s1 = __shfl_xor_sync(0xffffffffu, s1, 1);
+  if (b0) {
+    m0 = s0;
+    m2 = s1;
+  } else {
+    m1 = s0;
+    m3 = s1;
+  }
+}
+
+// A decoded unit into TMEM: 16 lanes (rows) x 32 columns (64 K, two bf16 per column, natural K order).
+// The decoder leaves lane 4g + t with the K pairs 8t .. 8t+7 of rows g and g + 8 (register 2s + rh = pair 8t + s
+// of row g + 8rh: the unit's lane layout).  The .16x128b.x8 store puts register i of lane 4g + t at row
+// g + 8 (i % 2), column 4 (i / 2) + t, i.e. lane t must hold the pairs 4c + t, c = 0..7.  Pair 4c + t lives in lane
+// c / 2 at s = 4 (c % 2) + t: for each half h = c % 2 and row rh that is a 4 x 4 transpose across the quad.
+MBP_DEV void tc_st_a(uint32_t taddr, const uint32_t (&A)[16], int t) {
+  uint32_t a[16];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int rh = 0; rh < 2; ++rh) {
+      uint32_t m0 = A[2 * (4 * h + 0) + rh], m1 = A[2 * (4 * h + 1) + rh], m2 = A[2 * (4 * h + 2) + rh],
+               m3 = A[2 * (4 * h + 3) + rh];
+      quad_transpose(m0, m1, m2, m3, t);  // now m_j = pair 4(2j + h) + t of row rh (column c = 2j + h)
+      a[2 * (2 * 0 + h) + rh] = m0;
+      a[2 * (2 * 1 + h) + rh] = m1;
+      a[2 * (2 * 2 + h) + rh] = m2;
+      a[2 * (2 * 3 + h) + rh] = m3;
+    }
   asm volatile(
       "tcgen05.st.sync.aligned.16x128b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
       "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]), "r"(a[8]), "r"(a[9]),
@@ -167,11 +185,14 @@ MBP_DEV void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-MBP_DEV void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+MBP_DEV void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
       : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -183,85 +204,64 @@ MBP_DEV void store_elem(const GemmParams& p, int tok, int row, float f) {
     reinterpret_cast<uint16_t*>(p.out)[(size_t)tok * p.ldo + row] = __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 
-// Stream-K ranges: CTA c owns items [start(c), start(c + 1)), start(c) = floor(c * U / G); owner(u) is the CTA
-// whose range holds item u (the largest c with start(c) <= u).
-MBP_DEV long long range_start(long long c, long long U, long long G) { return c * U / G; }
-MBP_DEV int range_owner(long long u, long long U, long long G) { return (int)(((u + 1) * G + U - 1) / U - 1); }
-
-// The part of CTA range [u0, u1) inside tile `tile`: chunks [cb, ce) of the tile.
-struct Seg {
-  int tile, cb, ce;
-};
-MBP_DEV Seg seg_of(int tile, int u0, int u1, int C) {
-  const int t0 = tile * C;
-  Seg s;
-  s.tile = tile;
-  s.cb = u0 > t0 ? u0 - t0 : 0;
-  s.ce = u1 < t0 + C ? u1 - t0 : C;
-  return s;
-}
-
-template <class CF>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ GemmParams p) {
-  constexpr int PS = CF::kPS, KC = CF::kKC, AS = CF::kAS, XS = CF::kXS, NACC = CF::kNAcc;
-  constexpr int kPackedStage = CF::kPackedStage;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* sm = smem_raw + (base - raw);
+  const GLayout L = gemm_layout(p.bn);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t bars = base + CF::kBars;
-  const uint32_t pfull = bars, pempty = pfull + 8 * PS;
-  const uint32_t afull = pempty + 8 * PS, aempty = afull + 8 * AS;
-  const uint32_t xfull = aempty + 8 * AS, xempty = xfull + 8 * XS;
-  const uint32_t accfull = xempty + 8 * XS, accempty = accfull + 16;
-  volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(sm + CF::kMisc);
-  volatile uint32_t* tmem_slot = misc;
-  volatile uint32_t* abort_word = misc + 1;  // set by the scheduler when a wait gave up
-  volatile int* ticket_word = reinterpret_cast<volatile int*>(misc + 2);
+  const uint32_t bars = base + L.bars;
+  const uint32_t pfull = bars, pempty = pfull + 8 * kPS;
+  const uint32_t afull = pempty + 8 * kPS, aempty = afull + 8 * kAS;
+  const uint32_t xfull = aempty + 8 * kAS, xempty = xfull + 8 * kXS;
+  const uint32_t done = xempty + 8 * kXS;
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sm + L.tmem_slot);
+  volatile uint32_t* abort_word = tmem_slot + 2;  // set by the scheduler when a wait gave up
   const int C = p.C;
-  const long long G = gridDim.x;
-  const int u0 = (int)range_start(blockIdx.x, p.U, G), u1 = (int)range_start(blockIdx.x + 1, p.U, G);
-  const int nit = u1 - u0;
-  const int tile_first = u0 / C, tile_last = (u1 - 1) / C;
-  const int nseg = tile_last - tile_first + 1;
-  const uint32_t acc_cols = (uint32_t)p.acc_cols;
-  const uint32_t a_col0 = NACC * acc_cols;  // TMEM-resident A ring (CF::kTA): AS stages of 32 columns
+  const int rb0 = blockIdx.x * 8;  // first row tile
+  const int tok0 = blockIdx.y * p.bn;
+  const int ks = blockIdx.z;       // K split index == cluster rank (cluster dims 1 x 1 x split)
+  const int cs = (int)((long long)ks * C / p.split), ce = (int)((long long)(ks + 1) * C / p.split);
+  const int nc = ce - cs;
+  // TMEM: the accumulator (acc_cols >= bn columns), then the decoded-A ring (kAS x 32 columns)
+  const uint32_t acc_cols = p.bn <= 32 ? 32 : p.bn <= 64 ? 64 : p.bn <= 128 ? 128 : 256;
+  uint32_t tmem_cols = 32;
+  while (tmem_cols < acc_cols + 32 * kAS) tmem_cols *= 2;
+  const uint32_t a_col0 = acc_cols;
 
   // Programmatic dependent launch: the packed weights never depend on the previous kernel of the stream, so the
-  // first stages' units are pulled into L2 while it drains; every thread waits for it before touching x or out.
-  if (warp == kWProdWarp && lane < 8) {  // the first weight stages' units, one contiguous run per row tile
-    const Seg sg = seg_of(tile_first, u0, u1, C);
-    const int rt = (sg.tile % p.R8) * 8 + lane, n = min(PS * KC, sg.ce - sg.cb);
-    if (rt < p.Rout) prefetch_l2(p.units + ((size_t)rt * C + sg.cb) * MBP_C12_UNIT_BYTES, (uint32_t)n * MBP_C12_UNIT_BYTES);
+  // first ring's units are pulled into L2 while it drains; every thread waits for it before touching x or out.
+  if (warp == 0 && lane < 8 * kPS) {
+    const int d = lane & 7, i = lane >> 3;
+    if (rb0 + d < p.Rout && i < nc)
+      prefetch_l2(p.units + ((size_t)(rb0 + d) * C + cs + i) * MBP_C12_UNIT_BYTES, MBP_C12_UNIT_BYTES);
   }
   grid_dep_wait();
   grid_dep_launch();
 
   if (tid == 0) {
-    for (int i = 0; i < PS; ++i) {
+    for (int i = 0; i < kPS; ++i) {
       mbar_init(pfull + 8 * i, 1);
-      mbar_init(pempty + 8 * i, kDecWarps * 32);
+      mbar_init(pempty + 8 * i, 8 * 32);
     }
-    for (int i = 0; i < AS; ++i) {
+    for (int i = 0; i < kAS; ++i) {
       mbar_init(afull + 8 * i, 8 * 32);
       mbar_init(aempty + 8 * i, 1);
     }
-    for (int i = 0; i < XS; ++i) {
+    for (int i = 0; i < kXS; ++i) {
       mbar_init(xfull + 8 * i, 1);
       mbar_init(xempty + 8 * i, 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(accfull + 8 * i, 1);
-      mbar_init(accempty + 8 * i, 4);
-    }
+    mbar_init(done, 1);
     *abort_word = 0u;
     fence_mbar_init();
+    prefetch_tmap(&p.wmap);
     prefetch_tmap(&p.xmap);
   }
-  if (warp == kMmaWarp) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(base + CF::kMisc),
-                 "r"((uint32_t)p.tcols)
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(base + L.tmem_slot),
+                 "r"(tmem_cols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -270,453 +270,325 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == kWProdWarp) {
+  if (warp == 0) {
     // ---------------- weight producer ----------------
-    // Stage uses walk the range as groups of up to KC consecutive items of one segment; lanes 0-7 each copy their
-    // row tile's KC units (contiguous in the row-tile-major layout) with one bulk copy.  (One 3-D tensor copy of
-    // the 8 units of an item per stage measured ~0.45 us per issue on B200, a limit of ~27 GB/s per SM.)
-    const uint64_t pol = policy_evict_first();
-    int use = 0;
-    bool ok = true;
-    for (int s = 0; s < nseg && ok; ++s) {
-      const Seg sg = seg_of(tile_first + s, u0, u1, C);
-      const int rb = sg.tile % p.R8, nr = min(8, p.Rout - rb * 8);
-      for (int c0 = sg.cb; c0 < sg.ce; c0 += KC, ++use) {
-        const int n = min(KC, sg.ce - c0), ps = use % PS;
-        if (use >= PS && !mbar_wait(pempty + 8 * ps, ((use / PS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) mbar_arrive_expect_tx(pfull + 8 * ps, (uint32_t)(nr * n * MBP_C12_UNIT_BYTES));
-        __syncwarp();
-        if (lane < nr)
-          bulk_g2s_hint(base + CF::kPacked + ps * kPackedStage + lane * KC * MBP_C12_UNIT_BYTES,
-                        p.units + ((size_t)(rb * 8 + lane) * C + c0) * MBP_C12_UNIT_BYTES,
-                        (uint32_t)n * MBP_C12_UNIT_BYTES, pfull + 8 * ps, pol);
+    if (lane == 0) {
+      for (int i = 0; i < nc; ++i) {
+        const int ps = i % kPS;
+        if (i >= kPS && !mbar_wait(pempty + 8 * ps, ((i / kPS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
+        mbar_arrive_expect_tx(pfull + 8 * ps, kPackedStage);
+        tma_load_3d(base + L.packed + ps * kPackedStage, &p.wmap, 0, cs + i, rb0, pfull + 8 * ps);
       }
     }
-    __syncwarp();
+    __syncwarp();  // lanes 1-31 wait here for the producing lane
   } else if (warp == kXWarp) {
     // ---------------- x producer ----------------
     if (lane == 0) {
-      for (int j = 0; j < nit; ++j) {
-        const int u = u0 + j;
-        const int tile = u / C, chunk = u - tile * C;
-        const int xs = j % XS;
-        if (j >= XS && !mbar_wait(xempty + 8 * xs, ((j / XS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
+      for (int i = 0; i < nc; ++i) {
+        const int xs = i % kXS;
+        if (i >= kXS && !mbar_wait(xempty + 8 * xs, ((i / kXS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
         mbar_arrive_expect_tx(xfull + 8 * xs, (uint32_t)p.bn * 128);
-        tma_load_2d(base + CF::kX + xs * CF::kXStage, &p.xmap, chunk * 64, (tile / p.R8) * p.bn, xfull + 8 * xs);
+        tma_load_2d(base + L.x + xs * p.bn * 128, &p.xmap, (cs + i) * 64, tok0, xfull + 8 * xs);
       }
     }
     __syncwarp();
   } else if (warp == kSchedWarp) {
     // ---------------- MMA scheduler ----------------
-    // Waits for item j's A and x stages (and, when j starts segment s >= NACC, for the epilogue to have released
-    // segment s-NACC's accumulator) while the issuer is still feeding item j-1 to the tensor pipe, then meets it on a
-    // named barrier.  Every round is always met, so a timed-out wait ends both warps' loops through the abort word
-    // instead of a missing partner.
+    // Waits for chunk i's A and x stages while the issuer is still feeding chunk i-1 to the tensor pipe, then
+    // meets it on a named barrier.  (An mbarrier wait in the issuing thread itself, right behind its MMAs and
+    // commits, measured ~300-450 cycles per chunk even on phases completed long before.)  Every round is
+    // always met, so a timed-out wait ends both warps' loops through the abort word instead of a missing partner.
     bool ok = true;
-    int s = 0;
-    int seg_end = (tile_first + 1) * C;
-    for (int j = 0; j < nit; ++j) {
-      const int u = u0 + j;
-      if (u == seg_end) {
-        ++s;
-        seg_end += C;
-      }
+    for (int i = 0; i < nc && !p.direct; ++i) {
       if (lane == 0 && ok) {
-        if (s >= NACC && u % C == 0)  // segment s reuses accumulator s % NACC: wait for segment s - NACC's epilogue
-          ok = mbar_wait(accempty + 8 * (s % NACC), ((s / NACC) - 1) & 1, MBP_DEV_TIMEOUT_MMA, p.wait_ns);
-        ok = ok && mbar_wait(afull + 8 * (j % AS), (j / AS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns) &&
-             mbar_wait(xfull + 8 * (j % XS), (j / XS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns);
+        ok = mbar_wait(afull + 8 * (i % kAS), (i / kAS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns) &&
+             mbar_wait(xfull + 8 * (i % kXS), (i / kXS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns);
         if (!ok) *abort_word = 1u;
       }
       named_bar_sync(kHandBar, 64);
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     const uint32_t idesc = idesc_bf16(p.bn);
     // descriptors of the first stages; the 14-bit start-address field (bytes >> 4) of a descriptor advances by
     // offset >> 4 without carrying out (shared addresses stay below 256 KB)
-    const uint64_t da0 = smem_desc_sw128(base + CF::kA), db0 = smem_desc_sw128(base + CF::kX);
-    int s = 0;
-    int seg_beg = u0, seg_end = (tile_first + 1) * C;
-    for (int j = 0; j < nit; ++j) {
-      const int u = u0 + j;
-      if (u == seg_end) {
-        ++s;
-        seg_beg = seg_end;
-        seg_end += C;
-      }
-      named_bar_sync(kHandBar, 64);  // the scheduler saw item j's stages full
-      if (lane == 0 && *abort_word == 0u) {
-        const int as = j % AS, xs = j % XS;
-        tc_fence_after();
-        const uint64_t da = da0 + (uint64_t)((as * kAStage) >> 4), db = db0 + (uint64_t)((xs * CF::kXStage) >> 4);
-        const uint32_t d = tmem + (uint32_t)(s % NACC) * acc_cols;
-        if constexpr (CF::kTA) {
-          const uint32_t ta = tmem + a_col0 + (uint32_t)as * 32u;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) tc_mma_ts(d, ta + 8 * k, db + 2 * k, idesc, (u != seg_beg || k != 0) ? 1u : 0u);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 4; ++k) tc_mma(d, da + 2 * k, db + 2 * k, idesc, (u != seg_beg || k != 0) ? 1u : 0u);
+    const uint64_t db0 = smem_desc_sw128(base + L.x);
+    for (int i = 0; i < nc; ++i) {
+      if (p.direct) {
+        // poll both stages with non-blocking probes (bounded; a timed-out wait ends the loop like an abort)
+        if (lane == 0 && *abort_word == 0u) {
+          const uint32_t fa = afull + 8 * (i % kAS), fx = xfull + 8 * (i % kXS);
+          const uint32_t pa = (i / kAS) & 1, px = (i / kXS) & 1;
+          uint64_t t0 = 0;
+          for (uint32_t spin = 0; !(mbar_test(fa, pa) && mbar_test(fx, px)); ++spin) {
+            if ((spin & 255u) == 255u) {
+              const uint64_t now = globaltimer();
+              if (t0 == 0) {
+                t0 = now;
+              } else if (now - t0 > p.wait_ns) {
+                set_status(MBP_DEV_TIMEOUT_FULL);
+                *abort_word = 1u;
+                break;
+              }
+            }
+          }
         }
+      } else {
+        named_bar_sync(kHandBar, 64);  // the scheduler saw chunk i's stages full
+      }
+      if (lane == 0 && *abort_word == 0u) {
+        const int as = i % kAS, xs = i % kXS;
+        tc_fence_after();
+        const uint32_t ta = tmem + a_col0 + (uint32_t)as * 32u;
+        const uint64_t db = db0 + (uint64_t)((xs * p.bn * 128) >> 4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) tc_mma_ts(tmem, ta + 8 * k, db + 2 * k, idesc, (i | k) != 0);
         tc_commit(aempty + 8 * as);
         tc_commit(xempty + 8 * xs);
-        // the segment's last item: the accumulator is complete once these MMAs are
-        if (u + 1 == seg_end || u + 1 == u1) tc_commit(accfull + 8 * (s % NACC));
       }
       __syncwarp();
     }
-  } else if (warp < kXWarp) {
-    // ---------------- decoders: group gi takes items gi, gi + kGroups, ... ----------------
-    // Row tile d of the 128-row tile.  With A in TMEM a warp may only write its lane quadrant (warp % 4), so row tile
-    // d (lanes 16d .. 16d+15) goes to a warp of quadrant d / 2: the warps of a group cover quadrants 2, 3, 0, 1 twice.
-    const int dw = warp - kDec0, gi = dw >> 3, di = dw & 7;
-    const int d = CF::kTA ? 2 * ((di + kDec0) & 3) + (di >> 2) : di;
-    const uint32_t xr = base + CF::kMask + dw * kMaskUnitBytes;
-    mask_clear(xr, kMaskUnitBytes, lane);
-    const int g = lane >> 2, t = lane & 3;
-    // shared-memory A: destination rows r = 16 d + 8 rh + g inside the 128-row A tile (SW128 K-major)
-    uint32_t dst[2][2];
-#pragma unroll
-    for (int rh = 0; rh < 2; ++rh) {
-      const int r = 16 * d + 8 * rh + g;
-      const uint32_t row = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
-      dst[rh][0] = row + ((uint32_t)((2 * t) ^ (r & 7)) << 4);
-      dst[rh][1] = row + ((uint32_t)((2 * t + 1) ^ (r & 7)) << 4);
-    }
-    // Every decoder warp waits on and releases every stage use; in a use of n items starting at item j0, group gi
-    // decodes the items j with j % kGroups == gi.
-    bool valid = false, ok = true;
+    if (lane == 0) tc_commit(done);  // fires when every issued MMA has completed
+    __syncwarp();
+  } else {
+    // ---------------- decoders: group gi takes local chunks gi, gi + kGroups, ... ----------------
+    // Row tile d of the 128-row tile.  A warp may only write its TMEM lane quadrant (warp % 4), so row tile d
+    // (lanes 16d .. 16d+15) goes to a warp of quadrant d / 2: the warps of a group cover quadrants 2, 3, 0, 1 twice.
+    const int dw = warp - 2, gi = dw >> 3, di = dw & 7;
+    const int d = 2 * ((di + 2) & 3) + (di >> 2);
+    const int rt = rb0 + d;
+    const bool valid = rt < p.Rout;
     uint32_t T0 = 0, T1 = 0;
     EscCursor cur;
-    int use = 0, j0 = 0;
-    for (int s = 0; s < nseg && ok; ++s) {
-      const Seg sg = seg_of(tile_first + s, u0, u1, C);
-      // a new segment: this warp's row tile, its table and its escape slice
-      const int rt = (sg.tile % p.R8) * 8 + d;
-      valid = rt < p.Rout;
-      T0 = T1 = 0;
-      if (valid) {
-        const uint32_t b = p.bases[rt];
-        T0 = table_lo(b);
-        T1 = table_hi(b);
-        cur.init(p.esc, p.esc_off[(size_t)rt * C + sg.cb], p.esc_off[(size_t)rt * C + sg.ce], lane);
+    const uint32_t xr = base + L.xr + dw * kMaskUnitBytes;
+    mask_clear(xr, kMaskUnitBytes, lane);
+    if (valid) {
+      const uint32_t b = p.bases[rt];
+      T0 = table_lo(b);
+      T1 = table_hi(b);
+      cur.init(p.esc, p.esc_off[(size_t)rt * C + cs], p.esc_off[(size_t)rt * C + ce], lane);
+    } else {
+      cur.init(p.esc, 0, 0, lane);
+    }
+    const int t = lane & 3;
+    for (int i = gi; i < nc; i += kGroups) {
+      const int ps = i % kPS, as = i % kAS;
+      if (!mbar_wait(pfull + 8 * ps, (i / kPS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns)) break;
+      const unsigned char* u = sm + L.packed + ps * kPackedStage + d * MBP_C12_UNIT_BYTES + lane * 16;
+      const uint4 p0 = *reinterpret_cast<const uint4*>(u);
+      const uint4 p1 = *reinterpret_cast<const uint4*>(u + 512);
+      const uint4 p2 = *reinterpret_cast<const uint4*>(u + 1024);
+      uint32_t A[16];
+      const uint32_t c = (uint32_t)(cs + i);
+      if (valid) cur.seek(c, lane);
+      if (valid && cur.next_chunk == c) {
+        uint32_t tgt[1] = {0u};
+        cur.scatter<1>(c, c + 1, xr, kMaskUnitBytes, lane, tgt);
+        __syncwarp();
+        uint4 m0, m1;
+        take_mask(xr, tgt[0], lane, m0, m1);
+        decode_unit_m(p0, p1, p2, T0, T1, m0, m1, A);
       } else {
-        cur.init(p.esc, 0, 0, lane);
+        decode_unit(p0, p1, p2, T0, T1, A);
       }
-      for (int c0 = sg.cb; c0 < sg.ce && ok; c0 += KC, ++use) {
-        const int n = min(KC, sg.ce - c0), ps = use % PS;
-        if (!mbar_wait(pfull + 8 * ps, (use / PS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns)) {
-          ok = false;
-          break;
-        }
-        uint32_t dep = 0;
-        for (int jj = (gi - j0 % kGroups + kGroups) % kGroups; jj < n; jj += kGroups) {
-          const int j = j0 + jj, as = j % AS;
-          const unsigned char* un =
-              sm + CF::kPacked + ps * kPackedStage + (d * KC + jj) * MBP_C12_UNIT_BYTES + lane * 16;
-          const uint4 p0 = *reinterpret_cast<const uint4*>(un);
-          const uint4 p1 = *reinterpret_cast<const uint4*>(un + 512);
-          const uint4 p2 = *reinterpret_cast<const uint4*>(un + 1024);
-          uint32_t A[16];
-          const uint32_t c = (uint32_t)(c0 + jj);
-          if (valid) cur.seek(c, lane);
-          if (valid && cur.next_chunk == c) {
-            uint32_t tgt[1] = {0u};
-            cur.scatter<1>(c, c + 1, xr, kMaskUnitBytes, lane, tgt);
-            __syncwarp();
-            uint4 m0, m1;
-            take_mask(xr, tgt[0], lane, m0, m1);
-            decode_unit_m(p0, p1, p2, T0, T1, m0, m1, A);
-          } else {
-            decode_unit(p0, p1, p2, T0, T1, A);
-          }
-          dep ^= A[0] ^ A[8];  // A[0] depends on p0 and p2, A[8] on p1
-          if (j >= AS && !mbar_wait(aempty + 8 * as, ((j / AS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) {
-            ok = false;
-            break;
-          }
-          if constexpr (CF::kTA) {
-            tc_st_a(tmem + ((uint32_t)(16 * d) << 16) + a_col0 + (uint32_t)as * 32u, A);
-            tc_fence_before();  // the stores are complete (wait::st) and ordered before the arrive
-          } else {
-            unsigned char* a = sm + CF::kA + as * kAStage;
+      // A[0] depends on p0 and p2, A[8] on p1: all three loads have returned before the stage is handed back
+      mbar_arrive_dep(pempty + 8 * ps, A[0] ^ A[8]);
+      if (i >= kAS && !mbar_wait(aempty + 8 * as, ((i / kAS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
+      tc_st_a(tmem + ((uint32_t)(16 * d) << 16) + a_col0 + (uint32_t)as * 32u, A, t);
+      tc_fence_before();  // the stores are complete (wait::st) and ordered before the arrive
+      mbar_arrive(afull + 8 * as);
+    }
+  }
+
+  // ---------------- epilogue: TMEM -> registers -> global (or a cluster reduction) ----------------
+  // Decoder warps own TMEM lane quadrant (warp % 4); the kDecWarps/4 warps of a quadrant split the columns.
+  const bool epi = warp >= 2 && warp < 2 + kDecWarps;
+  const int q = warp & 3, part = (warp - 2) >> 2, nparts = kDecWarps / 4;
+  const int ncol = (p.bn + 31) / 32;
+  const int row_l = q * 32 + lane;                 // row inside the 128-row tile
+  const int row = rb0 * 16 + row_l;                // global output row
+  bool ok = true;
+  if (epi) {
+    ok = mbar_wait(done, 0, MBP_DEV_TIMEOUT_MMA, p.wait_ns);
+    ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
+    tc_fence_after();
+  }
+  if (p.split == 1) {
+    if (epi && ok) {
+      for (int cc = part; cc < ncol; cc += nparts) {
+        uint32_t v[32];
+        tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32), v);
+        if (row < p.Rout * 16) {
 #pragma unroll
-            for (int rh = 0; rh < 2; ++rh) {
-              *reinterpret_cast<uint4*>(a + dst[rh][0]) = make_uint4(A[0 + rh], A[2 + rh], A[4 + rh], A[6 + rh]);
-              *reinterpret_cast<uint4*>(a + dst[rh][1]) = make_uint4(A[8 + rh], A[10 + rh], A[12 + rh], A[14 + rh]);
-            }
-            fence_async_smem();
+          for (int j = 0; j < 32; ++j) {
+            // columns past the tile's bn tokens (bn % 32 != 0) belong to the next token tile's CTA
+            const int tok = tok0 + cc * 32 + j;
+            if (cc * 32 + j < p.bn && tok < p.m) store_elem(p, tok, row, __uint_as_float(v[j]));
           }
-          mbar_arrive(afull + 8 * as);
         }
-        // this warp's loads from the stage have returned (dep) before the stage goes back to the producer
-        mbar_arrive_dep(pempty + 8 * ps, dep);
-        j0 += n;
       }
     }
   } else {
-    // ---------------- epilogue: TMEM -> registers -> the output, or a partial tile ----------------
-    const int q = warp & 3, et = tid - 32 * kEpi0;  // TMEM lane quadrant, thread index among the 128
-    const int row_l = q * 32 + lane;                 // row inside the 128-row tile
-    const int ncol = p.bn / 16;  // 16-column TMEM loads (bn % 16 == 0)
-    const size_t slot_elems = (size_t)p.bn * 128;
-    for (int s = 0; s < nseg; ++s) {
-      const Seg sg = seg_of(tile_first + s, u0, u1, C);
-      const int rb = sg.tile % p.R8, tok0 = (sg.tile / p.R8) * p.bn;
-      const int row = rb * 128 + row_l;
-      const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(s % NACC) * acc_cols;
-      bool ok = mbar_wait(accfull + 8 * (s % NACC), (s / NACC) & 1, MBP_DEV_TIMEOUT_MMA, p.wait_ns);
-      ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
-      tc_fence_after();
-      if (sg.cb == 0 && sg.ce == C) {
-        // the whole tile: store
-        for (int cc = 0; cc < ncol; ++cc) {
-          uint32_t v[16];
-          if (ok) tc_ld16(acc + (uint32_t)(cc * 16), v);
-          if (ok && row < p.Rout * 16) {
+    // Partial tiles go to shared memory column-major (element (r, c) at c*128 + r, conflict-free), the ring
+    // area being free once every MMA has completed; rank ks then sums columns [c0, c1) over the cluster.
+    float* red = reinterpret_cast<float*>(sm);
+    if (epi) {
+      for (int cc = part; cc < ncol; cc += nparts) {
+        uint32_t v[32];
+        if (ok) tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32), v);
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const int tok = tok0 + cc * 16 + jj;
-              if (tok < p.m) store_elem(p, tok, row, __uint_as_float(v[jj]));
-            }
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(accempty + 8 * (s % NACC));
-        continue;
-      }
-      // part of a split tile: the FP32 partial to this CTA's slot (column-major: element (r, col) at col*128 + r)
-      float* mine = p.ws_part + (size_t)(2 * blockIdx.x + (s == 0 ? 0 : 1)) * slot_elems;
-      for (int cc = 0; cc < ncol; ++cc) {
-        uint32_t v[16];
-        if (ok) tc_ld16(acc + (uint32_t)(cc * 16), v);
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj)
-          __stcg(mine + (size_t)(cc * 16 + jj) * 128 + row_l, ok ? __uint_as_float(v[jj]) : 0.f);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(accempty + 8 * (s % NACC));  // a later segment may reuse this accumulator
-      // ticket: the contributor that arrives last adds every part, in CTA order
-      __threadfence();
-      named_bar_sync(kEpiBar, 128);
-      const long long t0 = (long long)sg.tile * C;
-      const int c_lo = range_owner(t0, p.U, G), c_hi = range_owner(t0 + C - 1, p.U, G);  // its contributors
-      if (et == 0) *ticket_word = atomicAdd(p.ws_cnt + sg.tile, 1);
-      named_bar_sync(kEpiBar, 128);
-      if (*ticket_word == c_hi - c_lo) {
-        __threadfence();
-        // float4 f = rows 4*(f % 32) .. +3 of column f / 32: a warp reads one column's 128 rows per step.  The
-        // contributors are CTAs c_lo..c_hi; the tile is the first segment of each of them but c_lo, whose range may
-        // start in an earlier tile (then the tile is its last segment).  Loads of two contributors for two
-        // float4s are issued together (L2-resident partials), then added in CTA order.
-        const int ncols = min(p.bn, p.m - tok0), nf = ncols * 32;
-        const int lo_which = range_start(c_lo, p.U, G) >= t0 ? 0 : 1;
-        const float* part0 = p.ws_part + (size_t)(2 * c_lo + lo_which) * slot_elems;  // c_lo's slot
-        const float* part1 = p.ws_part + (size_t)(2 * (c_lo + 1)) * slot_elems;       // c_lo + 1 + i: part1 + 2i slots
-        for (int f0 = et; f0 < nf; f0 += 2 * 128) {
-          float4 sum[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int f = min(f0 + u * 128, nf - 1);
-            sum[u] = __ldcg(reinterpret_cast<const float4*>(part0 + (size_t)(f >> 5) * 128 + (f & 31) * 4));
-          }
-          for (int i0 = 0; i0 < c_hi - c_lo; i0 += 2) {
-            float4 v[2][2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int f = min(f0 + u * 128, nf - 1);
-#pragma unroll
-              for (int i = 0; i < 2; ++i)
-                if (i0 + i < c_hi - c_lo)
-                  v[u][i] = __ldcg(reinterpret_cast<const float4*>(part1 + (size_t)(2 * (i0 + i)) * slot_elems +
-                                                                   (size_t)(f >> 5) * 128 + (f & 31) * 4));
-            }
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-#pragma unroll
-              for (int i = 0; i < 2; ++i)
-                if (i0 + i < c_hi - c_lo) {
-                  sum[u].x += v[u][i].x;
-                  sum[u].y += v[u][i].y;
-                  sum[u].z += v[u][i].z;
-                  sum[u].w += v[u][i].w;
-                }
-          }
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int f = f0 + u * 128;
-            if (f >= nf) break;
-            const int col = f >> 5, grow = rb * 128 + (f & 31) * 4;
-            // Rout * 16 is a multiple of 16: four rows are all in or all out
-            if (grow >= p.Rout * 16) continue;
-            if (!p.vec_out) {
-              store_elem(p, tok0 + col, grow, sum[u].x);
-              store_elem(p, tok0 + col, grow + 1, sum[u].y);
-              store_elem(p, tok0 + col, grow + 2, sum[u].z);
-              store_elem(p, tok0 + col, grow + 3, sum[u].w);
-            } else if (p.f32out) {
-              *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)(tok0 + col) * p.ldo + grow) = sum[u];
-            } else {
-              const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(sum[u].x)) |
-                                  (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(sum[u].y)) << 16;
-              const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(sum[u].z)) |
-                                  (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(sum[u].w)) << 16;
-              *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.out) + (size_t)(tok0 + col) * p.ldo + grow) =
-                  make_uint2(lo, hi);
-            }
-          }
-        }
-        if (et == 0) p.ws_cnt[sg.tile] = 0;  // ready for the next call (ordered by the kernel boundary)
+        for (int j = 0; j < 32; ++j) red[(cc * 32 + j) * 128 + row_l] = ok ? __uint_as_float(v[j]) : 0.f;
       }
     }
+    __syncthreads();  // every role of this CTA is done before the cluster barrier
+    cluster_sync();
+    const int per = (ncol * 32 + p.split - 1) / p.split;
+    const int c0 = ks * per, c1 = min(ncol * 32, c0 + per);
+    const uint32_t raddr = smem_u32(red);
+    for (int idx = tid; idx < (c1 - c0) * 128; idx += kThreads) {
+      const int c = c0 + idx / 128, r = idx % 128;
+      float s = 0.f;
+      for (int rk = 0; rk < p.split; ++rk) {
+        float f;
+        asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                     : "=f"(f)
+                     : "r"(mapa(raddr + (uint32_t)(c * 128 + r) * 4, (uint32_t)rk)));
+        s += f;
+      }
+      const int tok = tok0 + c, grow = rb0 * 16 + r;
+      if (c < p.bn && tok < p.m && grow < p.Rout * 16) store_elem(p, tok, grow, s);
+    }
+    cluster_sync();  // keep this CTA's partials alive until every rank has read them
   }
-
   tc_fence_before();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)p.tcols)
-                 : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols) : "memory");
   }
 }
 
-using KernelFn = void (*)(GemmParams);
-
-template <class CF>
-KernelFn kernel_of() {
-  return reinterpret_cast<KernelFn>(&k_gemm<CF>);
-}
-
-struct Inst {
-  KernelFn fn;
-  int smem;
-  int nacc, tmem_a;  // accumulators; TMEM columns of the A ring (0: A in shared memory)
-};
-
-template <class CF>
-Inst inst() {
-  return Inst{kernel_of<CF>(), CF::kSmem, CF::kNAcc, CF::kTA ? CF::kAS * 32 : 0};
-}
-
-// The instance for a token tile of bn tokens (bn % 16 == 0, <= 256).
-// MBP_GEMM_CFG=<i> selects the i-th instance of the class (ring-depth sweeps).
-Inst pick(int bn) {
-  static const int sel = getenv("MBP_GEMM_CFG") ? atoi(getenv("MBP_GEMM_CFG")) : -1;
-  if (bn <= 32) {
-    switch (sel) {
-      case 0: return inst<CfgS0>();
-      case 2: return inst<CfgS2>();
-      default: return inst<CfgS1>();
-    }
-  }
-  if (bn <= 128) {
-    switch (sel) {
-      case 0: return inst<CfgM0>();
-      default: return inst<CfgM1>();
-    }
-  }
-  switch (sel) {
-    case 0: return inst<CfgL0>();
-    case 2: return inst<CfgL2>();
-    default: return inst<CfgL1>();
-  }
+// units [R][C][1536 bytes] viewed as a 3-D tensor of u64: {192, C, R}, box {192, 1, 8}
+bool encode_units_3d(CUtensorMap* map, const void* units, int R, int C) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {192, (cuuint64_t)C, (cuuint64_t)R};
+  const cuuint64_t strides[2] = {(cuuint64_t)MBP_C12_UNIT_BYTES, (cuuint64_t)C * MBP_C12_UNIT_BYTES};
+  const cuuint32_t box[3] = {192, 1, 8};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(units), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 std::mutex g_mu;
-std::map<std::pair<int, KernelFn>, bool> g_attr_done;
+std::map<int, bool> g_attr_done;
+std::map<std::tuple<int, int, int>, int> g_clusters;  // (device, split, smem) -> co-resident clusters
 
-int ensure_attr(KernelFn fn, int smem) {
+int ensure_attr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MBP_ERR_LAUNCH;
   std::lock_guard<std::mutex> lk(g_mu);
-  const auto key = std::make_pair(dev, fn);
-  if (g_attr_done.count(key)) return MBP_OK;
-  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-      cudaSuccess)
+  if (g_attr_done.count(dev)) return MBP_OK;
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_gemm), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kMaxSmem) != cudaSuccess)
     return MBP_ERR_SMEM;
-  g_attr_done[key] = true;
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_gemm), cudaFuncAttributeNonPortableClusterSizeAllowed,
+                           1) != cudaSuccess)
+    return MBP_ERR_CLUSTER;
+  g_attr_done[dev] = true;
   return MBP_OK;
 }
 
-int sm_count() {
+int co_resident_ctas(int split, int smem) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return sms;
-}
-
-// The decomposition of a call: token tile width, tiles, items and the grid.
-struct Plan {
-  int bn, R8, tiles, G, acc_cols;
-  long long U;
-};
-
-Plan make_plan(int n_out, int k, int m, int sms, bool streamk) {
-  Plan pl;
-  pl.bn = m >= 256 ? 256 : ((m + 15) / 16) * 16;
-  const int T = (m + pl.bn - 1) / pl.bn;
-  pl.R8 = (n_out / 16 + 7) / 8;
-  pl.tiles = pl.R8 * T;
-  const int C = k / 64;
-  pl.U = (long long)pl.tiles * C;
-  long long G = pl.tiles;  // whole tiles per CTA
-  if (streamk) {
-    // One CTA per SM, each with at least C / (parts - 1) items, so that a tile has at most `parts` contributors
-    // and the last one's fix-up (it re-reads the others' partial tiles) stays short: FP32 partials of wide token
-    // tiles are large, so those get fewer parts.
-    static const int parts_env = getenv("MBP_GEMM_PARTS") ? atoi(getenv("MBP_GEMM_PARTS")) : 0;
-    const int parts = parts_env >= 2 && parts_env <= kMaxParts ? parts_env : pl.bn <= 64 ? 8 : 4;
-    const long long min_items = (C + parts - 2) / (parts - 1);
-    G = pl.U / min_items;
-    if (G > sms) G = sms;
-    if (G < 1) G = 1;
+  const auto key = std::make_tuple(dev, split, smem);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_clusters.find(key);
+    if (it != g_clusters.end()) return it->second;
   }
-  pl.G = (int)G;
-  pl.acc_cols = pl.bn <= 32 ? 32 : ((pl.bn + 31) / 32) * 32;  // accumulator columns
-  return pl;
+  int ctas = sms;
+  if (split > 1) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, split);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = split;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    ctas = cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(&k_gemm), &cfg) == cudaSuccess
+               ? clusters * split
+               : 0;
+    cudaGetLastError();
+  }
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_clusters[key] = ctas;
+  return ctas;
 }
 
-// Workspace of a stream-K plan: a fixed region of tickets (one int per tile) that every shape places at the same
-// offset -- a workspace shared by calls of different shapes must never see one call's partial tiles land on
-// another call's tickets -- then two partial-tile slots per CTA.
-constexpr int kMaxTickets = 16384;
-constexpr size_t kTicketBytes = (size_t)kMaxTickets * 4;
-
-size_t ws_bytes_for(const Plan& pl) {
-  if (pl.G == pl.tiles) return 0;  // every CTA takes exactly one whole tile
-  return kTicketBytes + (size_t)2 * pl.G * pl.bn * 128 * 4;
+// K split: the largest cluster (<= 8, >= 4 chunks per CTA) whose tiles still fit one wave of co-resident CTAs,
+// when the tile count alone leaves more than a quarter of the SMs idle.
+int choose_split(int tiles, int C, int smem) {
+  int sms = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (tiles * 4 >= sms * 3) return 1;
+  int best = 1;
+  for (int s = 2; s <= 8; ++s) {
+    if (C / s < 4) break;
+    const int cap = co_resident_ctas(s, smem);
+    if (cap >= tiles * s && tiles * s <= sms) best = s;
+  }
+  return best;
 }
 
-int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out, int ldo, bool f32, void* ws,
-                size_t ws_bytes, cudaStream_t stream) {
+int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out, int ldo, bool f32,
+                cudaStream_t stream) {
   if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
   if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n || n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
   if (m < 1) return MBP_ERR_M;
   if (ldo < n_out) return MBP_ERR_SHAPE;
-  if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u) || ((uintptr_t)ws & 255u)) return MBP_ERR_ALIGN;
-  const int sms = sm_count();
-  static const bool no_split = getenv("MBP_GEMM_PARTS") && atoi(getenv("MBP_GEMM_PARTS")) == 1;
-  Plan pl = make_plan(n_out, w->k, m, sms, !no_split);
-  if (pl.U > 0x7fffffffLL / 2) return MBP_ERR_SHAPE;  // items are indexed with 32-bit integers
-  // no (or a too small) workspace, or more tiles than tickets: whole tiles per CTA
-  if (!ws || ws_bytes < ws_bytes_for(pl) || pl.tiles > kMaxTickets) pl = make_plan(n_out, w->k, m, sms, false);
-  const Inst in = pick(pl.bn);
-  int tcols = 32;  // TMEM: the accumulators, then the A ring of a TMEM-resident instance
-  while (tcols < in.nacc * pl.acc_cols + in.tmem_a) tcols *= 2;
-  if (tcols > 512) return MBP_ERR_SMEM;
-  int rc = ensure_attr(in.fn, in.smem);
+  if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u)) return MBP_ERR_ALIGN;
+  // Token tile: all tokens up to 256.  Short K (<= 2048): a cluster split-K's reduction costs more than its
+  // short main loop saves, so smaller token tiles fill the SMs instead, down to 64 while one wave holds them
+  // (measured at M=256: o 8192x1024 11.5 us with 128-token tiles against 16.9 us with a 2-way K split).
+  int bn = m >= 256 ? 256 : ((m + 15) / 16) * 16;
+  if (w->k / 64 <= 32) {
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int row_blocks = (n_out / 16 + 7) / 8;
+    int ntok = (m + bn - 1) / bn;
+    for (;;) {  // double the token tiles (balanced, multiples of 16 tokens) while they stay >= 64 and one wave
+      const int t2 = 2 * ntok, bn2 = ((m + t2 - 1) / t2 + 15) / 16 * 16;
+      if (bn2 < 64 || row_blocks * ((m + bn2 - 1) / bn2) > sms) break;
+      ntok = t2;
+      bn = bn2;
+    }
+  }
+  const GLayout L = gemm_layout(bn);
+  const int smem = L.total + 1024;
+  if (smem > kMaxSmem) return MBP_ERR_SMEM;
+  // the cluster reduction reuses the ring area for a 128 x bn FP32 tile
+  if (128 * ((bn + 31) / 32) * 32 * 4 > L.xr) return MBP_ERR_SMEM;
+  int rc = ensure_attr();
   if (rc) return rc;
   GemmParams p;
-  const int C = w->k / 64;
-  if (!encode_bf16_2d_cached(&p.xmap, x, (uint64_t)m, (uint64_t)w->k, (uint64_t)w->k, (uint32_t)pl.bn, 64u,
+  const int R = w->n / 16, C = w->k / 64;
+  const TmapKey wkey{w->units, (uint64_t)R, (uint64_t)C, 0, 0, 0, 0x200u};
+  if (!cached_map(&p.wmap, wkey, [&](CUtensorMap* mp) { return encode_units_3d(mp, w->units, R, C); }))
+    return MBP_ERR_TMAP;
+  if (!encode_bf16_2d_cached(&p.xmap, x, (uint64_t)m, (uint64_t)w->k, (uint64_t)w->k, (uint32_t)bn, 64u,
                              CU_TENSOR_MAP_SWIZZLE_128B))
     return MBP_ERR_TMAP;
   p.units = w->units;
@@ -724,27 +596,23 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   p.esc_off = w->esc_off;
   p.esc = w->esc;
   p.out = out;
-  const bool split = pl.G != pl.tiles;
-  p.ws_cnt = split ? static_cast<int*>(ws) : nullptr;
-  p.ws_part = split ? reinterpret_cast<float*>(static_cast<char*>(ws) + kTicketBytes) : nullptr;
-  p.U = pl.U;
   p.C = C;
   p.Rout = n_out / 16;
-  p.R8 = pl.R8;
   p.m = m;
   p.ldo = ldo;
-  p.bn = pl.bn;
+  p.bn = bn;
   p.f32out = f32 ? 1 : 0;
-  p.vec_out = ((uintptr_t)out & 15u) == 0 && ldo % 8 == 0;
-  p.tcols = tcols;
-  p.acc_cols = pl.acc_cols;
   p.wait_ns = wait_limit_ns();
+  static const bool direct = getenv("MBP_GEMM_DIRECT") != nullptr;
+  p.direct = direct ? 1 : 0;
+  const int tiles = ((p.Rout + 7) / 8) * ((m + bn - 1) / bn);
+  p.split = choose_split(tiles, C, smem);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.G);
+  cfg.gridDim = dim3((p.Rout + 7) / 8, (m + bn - 1) / bn, p.split);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = in.smem;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int na = 0;
   static const bool pdl = getenv("MBP_NO_PDL") == nullptr;  // MBP_NO_PDL set: plain stream serialisation
   if (pdl) {
@@ -752,28 +620,30 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
   }
+  if (p.split > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = p.split;
+    ++na;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, in.fn, p) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+  return cudaLaunchKernelEx(&cfg, k_gemm, p) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
 }
 
 }  // namespace
 
 extern "C" {
 
-size_t mbp_gemm_workspace(int n_out, int k, int m) {
-  if (n_out <= 0 || n_out % 16 || k <= 0 || k % 64 || m < 1) return 0;
-  return ws_bytes_for(make_plan(n_out, k, m, sm_count(), true));
+int mbp_gemm_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo,
+                 cudaStream_t stream) {
+  return gemm_launch(w, x, m, n_out, out, ldo, false, stream);
 }
 
-int mbp_gemm_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t* out, int ldo, void* workspace,
-                 size_t workspace_bytes, cudaStream_t stream) {
-  return gemm_launch(w, x, m, n_out, out, ldo, false, workspace, workspace_bytes, stream);
-}
-
-int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo, void* workspace,
-                     size_t workspace_bytes, cudaStream_t stream) {
-  return gemm_launch(w, x, m, n_out, out, ldo, true, workspace, workspace_bytes, stream);
+int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
+                     cudaStream_t stream) {
+  return gemm_launch(w, x, m, n_out, out, ldo, true, stream);
 }
 
 }  // extern "C"

@@ -88,9 +88,8 @@ SIGNATURES = [
                            _P]),
     ("mbp_gemv_c12_tp", _I, [ctypes.POINTER(C12), _P, _I, _I, ctypes.POINTER(TPExchange), _P, ctypes.POINTER(Geom),
                              _P]),
-    ("mbp_gemm_workspace", _SZ, [_I, _I, _I]),
-    ("mbp_gemm_c12", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P, _SZ, _P]),
-    ("mbp_gemm_c12_f32", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P, _SZ, _P]),
+    ("mbp_gemm_c12", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
+    ("mbp_gemm_c12_f32", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
 ]
 
 _lib = None

@@ -167,28 +167,9 @@ def gemv(p: PackedC12, x: torch.Tensor, n_out: int | None = None, out: torch.Ten
     return out
 
 
-_WORKSPACES: dict = {}
-
-
-def gemm_workspace(n_out: int, k: int, m: int, device=None) -> torch.Tensor:
-    """The zero-filled workspace the tensor-core path splits its tiles through, one per (device, stream), grown
-    on demand.  The kernels leave its tickets at zero, so it is reused as is; calls on one stream are ordered, and
-    calls on different streams get different workspaces."""
-    nbytes = int(lib().mbp_gemm_workspace(n_out, k, m))
-    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    key = (dev.index, _stream(dev))
-    ws = _WORKSPACES.get(key)
-    if ws is None or ws.numel() < nbytes:
-        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
-        _WORKSPACES[key] = ws
-    return ws
-
-
 def gemm(p: PackedC12, x: torch.Tensor, n_out: int | None = None, out: torch.Tensor | None = None,
-         out_dtype=torch.bfloat16, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """out[m, n_out] = x . W[:n_out]^T on the tcgen05 tensor cores (replaces S:783/979/1547/2985 and the
-    16-32-token register-A GEMMs S:2395).  `workspace`: a zero-filled uint8 tensor of at least
-    mbp_gemm_workspace bytes (default: the per-stream cached one)."""
+         out_dtype=torch.bfloat16) -> torch.Tensor:
+    """out[m, n_out] = x . W[:n_out]^T through the tcgen05 verify GEMM (replaces S:783/979/1547/2985)."""
     n_out = p.n if n_out is None else n_out
     _check_x(x, p.k, p.units.device)
     m = x.shape[0]
@@ -198,11 +179,9 @@ def gemm(p: PackedC12, x: torch.Tensor, n_out: int | None = None, out: torch.Ten
         raise ValueError("bad out tensor")
     if out.dtype not in (torch.float32, torch.bfloat16):
         raise ValueError(f"unsupported output dtype {out.dtype}")
-    if workspace is None:
-        workspace = gemm_workspace(n_out, p.k, m, x.device)
     fn = lib().mbp_gemm_c12_f32 if out.dtype == torch.float32 else lib().mbp_gemm_c12
-    check(fn(ctypes.byref(p.desc), x.data_ptr(), m, n_out, out.data_ptr(), out.stride(0), _ptr(workspace),
-             workspace.numel(), _stream(x.device)), "mbp_gemm_c12")
+    check(fn(ctypes.byref(p.desc), x.data_ptr(), m, n_out, out.data_ptr(), out.stride(0), _stream(x.device)),
+          "mbp_gemm_c12")
     return out
 
 

@@ -122,24 +122,20 @@ def test_gemm_repeated_calls_stage_reuse(shape):
         assert torch.allclose(o, ref, rtol=1e-2, atol=1e-2)
 
 
-@pytest.mark.parametrize("m", [16, 32, 128, 256])
-def test_gemm_streamk_deterministic(m):
-    """Split tiles are summed by their last contributor in CTA order, so repeated calls give identical bits; the
-    whole-tile decomposition (no workspace) sums in another order and agrees to FP32 rounding."""
+@pytest.mark.parametrize("shape,m", [((2048, 6144), 128), ((6144, 1536), 256), ((1536, 6144), 256),
+                                     ((14336, 6144), 256)])
+def test_gemm_deterministic(shape, m):
+    """Cluster split-K partials are added in a fixed order: repeated calls give identical bits."""
     import mbp
-    w = weight(2048, 6144, seed=51, escape_frac=0.005)
+    w = weight(*shape, seed=51, escape_frac=0.005)
     p = mbp.pack_c12(w)
-    x = tokens(m, 6144, seed=52)
-    ref = ref_f32(x, w)
+    x = tokens(m, shape[1], seed=52)
     a = mbp.gemm(p, x, out_dtype=torch.float32)
     b = mbp.gemm(p, x, out_dtype=torch.float32)
-    whole = mbp.gemm(p, x, out_dtype=torch.float32, workspace=torch.empty(0, dtype=torch.uint8, device="cuda"))
     torch.cuda.synchronize()
     assert mbp.device_status() == 0
     assert torch.equal(a, b)
-    assert torch.allclose(a, whole, rtol=1e-4, atol=1e-3)
-    assert torch.allclose(a, ref, rtol=1e-3, atol=1e-2)
-    assert_close_bf16(mbp.gemm(p, x), ref)
+    assert torch.allclose(a, ref_f32(x, w), rtol=1e-3, atol=1e-2)
 
 
 @pytest.mark.parametrize("layer", ["qkv_gate", "o"])
@@ -158,23 +154,3 @@ def test_gemm_decode_shapes(layer, m, variant):
     ref = ref_f32(x, w)
     assert_close_bf16(out, ref)
     assert_reference_norms(out, ref)
-
-
-def test_gemm_workspace_shared_across_shapes():
-    """One workspace serves calls of different shapes in any order: wide token tiles (large partial tiles) and
-    then a shape with many tiles, whose tickets must still start at zero; every call leaves the tickets zero."""
-    import mbp
-    from mbp.ops import gemm_workspace
-    a = weight(2048, 6144, seed=61)
-    b = weight(14336, 6144, seed=62)
-    pa, pb = mbp.pack_c12(a), mbp.pack_c12(b)
-    for m_a, m_b in ((256, 9), (128, 16), (256, 32)):
-        xa, xb = tokens(m_a, 6144, seed=m_a), tokens(m_b, 6144, seed=m_b + 1)
-        oa = mbp.gemm(pa, xa)
-        ob = mbp.gemm(pb, xb)
-        torch.cuda.synchronize()
-        assert mbp.device_status() == 0
-        assert_close_bf16(oa, ref_f32(xa, a))
-        assert_close_bf16(ob, ref_f32(xb, b))
-    ws = gemm_workspace(14336, 6144, 9)
-    assert int(ws[: 64 * 1024].view(torch.int32).abs().sum()) == 0

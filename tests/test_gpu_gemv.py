@@ -72,23 +72,26 @@ def test_every_token_count_small(m):
 @pytest.mark.parametrize("m", [1, 8, 16, 32])
 @pytest.mark.parametrize("frac", [0.0, 0.01])
 def test_baseline_config2(shape, m, frac):
-    """The decode shapes against the FP32 reference and the C oracle on a row sample."""
+    """The decode shapes against the FP32 reference and, over the whole output, the C oracle (which decodes the
+    packed bytes on the host and accumulates in FP32); both the GEMV and the public kernel_fn route."""
     import mbp
     w = weight(*shape, seed=0, escape_frac=frac)
-    p = mbp.pack_c12(w)
+    st = mbp.prepare({"o": w})
+    p = st["layers"]["o"]
     x = tokens(m, shape[1], seed=1)
     out = mbp.gemv(p, x)
+    api = mbp.kernel_fn({"x": x, "config": {"m": m, "n": shape[0], "k": shape[1], "layer": "o"}}, st)
     torch.cuda.synchronize()
     assert mbp.device_status() == 0
     ref = ref_f32(x, w)
-    assert_close_bf16(out, ref)
-    assert_reference_norms(out, ref)
-    # oracle: decode the packed bytes on the CPU and accumulate in FP32, rows [1024, 1536)
+    for o in (out, api):
+        assert_close_bf16(o, ref)
+        assert_reference_norms(o, ref)
     host = {"n": p.n, "k": p.k, "units": p.units.cpu().numpy(), "bases": p.bases.cpu().numpy(),
             "esc_off": p.esc_off.cpu().numpy(), "esc": p.esc.cpu().numpy().view(np.uint32)}
-    of, ob = oracle.gemv_packed(bits_np(x), host, row0=1024, nrows=512)
-    got = out[:, 1024:1536].float().cpu().numpy()
-    assert np.allclose(got, of[:, 1024:1536], rtol=1e-2, atol=1e-2)
+    of, ob = oracle.gemv_packed(bits_np(x), host)
+    for o in (out, api):
+        assert np.allclose(o.float().cpu().numpy(), of, rtol=1e-2, atol=1e-2)
 
 
 @pytest.mark.parametrize("m", [33, 64, 128, 256])
