@@ -64,20 +64,7 @@ struct __align__(64) GemmParams {
   int C, Rout, m, ldo, bn, split;
   int f32out;
   unsigned long long wait_ns;  // limit of every bounded wait
-  int direct;                  // the issuer polls the stage barriers itself (no scheduler hand-over)
 };
-
-// Non-blocking probe of an mbarrier phase.
-MBP_DEV bool mbar_test(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
 
 struct GLayout {
   int packed, a, x, xr, bars, tmem_slot, total;
@@ -299,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     // commits, measured ~300-450 cycles per chunk even on phases completed long before.)  Every round is
     // always met, so a timed-out wait ends both warps' loops through the abort word instead of a missing partner.
     bool ok = true;
-    for (int i = 0; i < nc && !p.direct; ++i) {
+    for (int i = 0; i < nc; ++i) {
       if (lane == 0 && ok) {
         ok = mbar_wait(afull + 8 * (i % kAS), (i / kAS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns) &&
              mbar_wait(xfull + 8 * (i % kXS), (i / kXS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns);
@@ -314,28 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     // offset >> 4 without carrying out (shared addresses stay below 256 KB)
     const uint64_t db0 = smem_desc_sw128(base + L.x);
     for (int i = 0; i < nc; ++i) {
-      if (p.direct) {
-        // poll both stages with non-blocking probes (bounded; a timed-out wait ends the loop like an abort)
-        if (lane == 0 && *abort_word == 0u) {
-          const uint32_t fa = afull + 8 * (i % kAS), fx = xfull + 8 * (i % kXS);
-          const uint32_t pa = (i / kAS) & 1, px = (i / kXS) & 1;
-          uint64_t t0 = 0;
-          for (uint32_t spin = 0; !(mbar_test(fa, pa) && mbar_test(fx, px)); ++spin) {
-            if ((spin & 255u) == 255u) {
-              const uint64_t now = globaltimer();
-              if (t0 == 0) {
-                t0 = now;
-              } else if (now - t0 > p.wait_ns) {
-                set_status(MBP_DEV_TIMEOUT_FULL);
-                *abort_word = 1u;
-                break;
-              }
-            }
-          }
-        }
-      } else {
-        named_bar_sync(kHandBar, 64);  // the scheduler saw chunk i's stages full
-      }
+      named_bar_sync(kHandBar, 64);  // the scheduler saw chunk i's stages full
       if (lane == 0 && *abort_word == 0u) {
         const int as = i % kAS, xs = i % kXS;
         tc_fence_after();
@@ -603,8 +569,6 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   p.bn = bn;
   p.f32out = f32 ? 1 : 0;
   p.wait_ns = wait_limit_ns();
-  static const bool direct = getenv("MBP_GEMM_DIRECT") != nullptr;
-  p.direct = direct ? 1 : 0;
   const int tiles = ((p.Rout + 7) / 8) * ((m + bn - 1) / bn);
   p.split = choose_split(tiles, C, smem);
   cudaLaunchConfig_t cfg = {};
