@@ -869,6 +869,13 @@ constexpr Tuned kTunedHilo[] = {
     {16, 128, 1, 0, {1, 1, 8, 2, 4, 2, 16}},    {16, 128, 2, 0, {1, 1, 8, 3, 3, 2, 16}},
     {16, 128, 4, 0, {2, 2, 16, 4, 1, 2, 9}},    {16, 128, 4, 0, {2, 2, 6, 3, 3, 2, 8}, 2},
     {16, 128, 4, 0, {2, 2, 4, 4, 2, 2, 8}, 4},  {16, 128, 4, 0, {4, 2, 4, 2, 2, 2, 4}, 8},
+    // the BASELINE router (256 x 6144), M = 1-8 / 9-16 / 17-32 and 64 / 128 / 256 tokens: 4.51 / 4.89 / 5.79 and
+    // 6.91 / 8.38 / 10.82 us against the planner's 9.06 / 9.50 / 6.94 and 13.6 / 9.73 / 13.5 us (exhaustive sweep;
+    // only geometries within half the 1e-5 tolerance against FP64: a warp that alone accumulates all 6144 columns
+    // of a row in FP32 can exceed it)
+    {16, 96, 1, 0, {1, 1, 8, 2, 4, 2, 16}},     {16, 96, 2, 0, {1, 1, 8, 2, 4, 2, 16}},
+    {16, 96, 4, 0, {2, 2, 16, 3, 1, 2, 8}},     {16, 96, 4, 0, {2, 2, 6, 4, 2, 2, 8}, 2},
+    {16, 96, 4, 0, {2, 2, 4, 4, 2, 2, 8}, 4},   {16, 96, 4, 0, {2, 2, 8, 2, 1, 2, 8}, 8},
 };
 
 std::mutex g_plan_mu;
