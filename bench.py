@@ -139,8 +139,26 @@ class Clocks:
                                       stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
-        time.sleep(0.2)
+        # nvidia-smi takes a moment to start: wait for its first row (at most 5 s) so that the samples cover
+        # the load that follows
+        t0 = time.time()
+        while self.p is not None and time.time() - t0 < 5.0:
+            self.f.flush()
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.02)
         return self
+
+    @staticmethod
+    def load(run, seconds: float = 0.3):
+        """Keeps the GPU under the timed work's load (untimed repetitions of `run`) for about `seconds`, so that
+        the clock samples taken around a short timed region see the clocks of that load."""
+        import torch
+        t0 = time.time()
+        while time.time() - t0 < seconds:
+            for _ in range(10):
+                run()
+            torch.cuda.synchronize()
 
     def __exit__(self, *a):
         if self.p is not None:
@@ -167,7 +185,8 @@ class Clocks:
                 continue
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm),
+                "window": "the timed region plus ~0.3 s of the same replays before and after it"}
 
 
 def _bits(w):
@@ -374,12 +393,14 @@ def run_mbp(args, rank, world):
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     with Clocks(dev.index) as clk:
+        Clocks.load(g_step.replay)
         torch.cuda.synchronize()
         a.record()
         for _ in range(args.steps):
             g_step.replay()
         b.record()
         torch.cuda.synchronize()
+        Clocks.load(g_step.replay)
     clocks = clk.summary()
     step_ms = a.elapsed_time(b) / args.steps
     assert mbp.device_status() == 0, "device status word set during the timed region"
@@ -682,6 +703,8 @@ def run_mbp_tp(args, rank, world):
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     with Clocks(dev.index) as clk:
+        for _ in range(600):  # the same load on every rank (a fixed count keeps the ranks' collectives in step)
+            run()
         dist.barrier()
         torch.cuda.synchronize()
         a.record()
@@ -690,6 +713,9 @@ def run_mbp_tp(args, rank, world):
         b.record()
         torch.cuda.synchronize()
         dist.barrier()
+        for _ in range(600):
+            run()
+        torch.cuda.synchronize()
     clocks = clk.summary()
     t = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
