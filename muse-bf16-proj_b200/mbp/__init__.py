@@ -18,7 +18,7 @@ from typing import TypedDict
 
 import torch
 
-from . import store
+from . import ops, store
 from ._lib import MbpError, device_status, lib, set_wait_limit
 from .ops import (BASE_MATRIX, BASE_TILE, PackedC12, PackedHiLo, gemm, gemv, gemv_plan, pack_c12, pack_hilo,
                   router, router_topk, unpack_c12)
@@ -92,21 +92,23 @@ def kernel_fn(data: Inputs, state: dict) -> torch.Tensor:
     x = data["x"]
     cfg = data["config"]
     layer, n = cfg["layer"], int(cfg["n"])
-    if x.dim() != 2 or x.dtype != torch.bfloat16 or not x.is_cuda:
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_cuda:
         raise ValueError("x must be a 2-D bf16 CUDA tensor")
     if not x.is_contiguous():
         x = x.contiguous()
-    if layer in state["hilo"]:
-        p = state["hilo"][layer]
-        if n != p.n:
-            raise ValueError(f"router output width {n} != {p.n}")
-        return router(p, x)
     p = state["layers"].get(layer)
     if p is None:
+        if layer in state["hilo"]:
+            h = state["hilo"][layer]
+            if n != h.n:
+                raise ValueError(f"router output width {n} != {h.n}")
+            return router(h, x)
         raise KeyError(f"layer {layer!r} was not prepared")
     if not 0 < n <= p.n or n % 16:
         raise ValueError(f"n={n} must be a multiple of 16 in (0, {p.n}]")
-    return gemv(p, x, n_out=n) if x.shape[0] <= GEMV_MAX_M else gemm(p, x, n_out=n)
+    if x.shape[1] != p.k or x.device != p.units.device or x.data_ptr() % 16:
+        ops._check_x(x, p.k, p.units.device)  # raises with the reason
+    return ops.project(p, x, n, x.shape[0] > GEMV_MAX_M)
 
 
 def route(data: Inputs, state: dict, k: int, renorm: bool = True) -> tuple[torch.Tensor, torch.Tensor]:

@@ -44,6 +44,7 @@ class PackedC12:
     def __post_init__(self):
         self.desc = C12(self.units.data_ptr(), self.bases.data_ptr(), self.esc_off.data_ptr(),
                         self.esc.data_ptr() if self.n_esc else 0, self.n, self.k, self.n_esc)
+        self.desc_ptr = ctypes.pointer(self.desc)  # reused by every call (no per-call ctypes wrapper)
 
     @property
     def nbytes(self) -> int:
@@ -78,6 +79,22 @@ class PackedHiLo:
     @property
     def payload_bytes(self) -> int:
         return self.units.numel()
+
+
+def project(p: PackedC12, x: torch.Tensor, n_out: int, tensor_cores: bool) -> torch.Tensor:
+    """The per-call fast path of ``kernel_fn``: a new BF16 [m, n_out] output from the GEMV or the tcgen05 GEMM.
+    The caller has checked x (contiguous BF16 [m, k] CUDA tensor on the weights' device) and n_out."""
+    m = x.shape[0]
+    dev = x.device
+    out = torch.empty((m, n_out), dtype=torch.bfloat16, device=dev)
+    L = lib()
+    if tensor_cores:
+        rc = L.mbp_gemm_c12(p.desc_ptr, x.data_ptr(), m, n_out, out.data_ptr(), n_out, _stream(dev))
+    else:
+        rc = L.mbp_gemv_c12(p.desc_ptr, x.data_ptr(), m, n_out, out.data_ptr(), n_out, None, _stream(dev))
+    if rc:
+        check(rc, "mbp_gemm_c12" if tensor_cores else "mbp_gemv_c12")
+    return out
 
 
 def _check_weight(w: torch.Tensor, dtype) -> None:
