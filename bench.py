@@ -534,28 +534,36 @@ def run_mbp(args, rank, world):
     assert mbp.device_status() == 0
 
     # ---------------- e2e through the public API with host buffers ----------------
-    # Each call: its x travels host -> device on a copy stream, kernel_fn runs on the compute stream as soon as
-    # that copy lands, and its output travels device -> host on a second copy stream, so the 32 copies of a step
-    # overlap the kernels of the other calls (a serving loop's usual double-buffering); the step ends when the
-    # last output is on the host.
+    # Each call's x travels host -> device on a copy stream into that call's input buffer (a serving loop's
+    # preallocated staging), kernel_fn runs on the compute stream once its copy has landed (an event per call),
+    # and its output travels device -> host on a second copy stream once the kernel is done, so the 32 copies of
+    # a step overlap the kernels of the other calls; the step ends when the last output is on the host.  The host
+    # issues each group of copies under one stream switch, and the outputs stay referenced until the compute
+    # stream has joined the device -> host stream, so no cross-stream allocator bookkeeping is needed.
     h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
+    x_in = [torch.empty(c[7].shape, dtype=c[7].dtype, device=dev) for c in calls]
+    ev_in = [torch.cuda.Event() for _ in calls]
+    ev_out = [torch.cuda.Event() for _ in calls]
+    api_calls = [(x_in[i], ev_in[i], ev_out[i], states[(c[1], c[2])],
+                  {"m": c[3], "n": c[4].n, "k": c[4].k, "layer": c[1]}) for i, c in enumerate(calls)]
 
     def api_step():
         comp = torch.cuda.current_stream()
-        h2d_s.wait_stream(comp)
+        h2d_s.wait_stream(comp)  # the previous step's kernels have read the input buffers
         d2h_s.wait_stream(comp)
-        for c in calls:
-            st = states[(c[1], c[2])]
-            with torch.cuda.stream(h2d_s):
-                xd = c[7].to(dev, non_blocking=True)
-            comp.wait_stream(h2d_s)
-            xd.record_stream(comp)
-            out = mbp.kernel_fn({"x": xd, "config": {"m": c[3], "n": c[4].n, "k": c[4].k, "layer": c[1]}}, st)
-            d2h_s.wait_stream(comp)
-            with torch.cuda.stream(d2h_s):
-                c[8].copy_(out, non_blocking=True)
-            out.record_stream(d2h_s)
-        comp.wait_stream(h2d_s)
+        with torch.cuda.stream(h2d_s):
+            for c, (xd, ei, _, _, _) in zip(calls, api_calls):
+                xd.copy_(c[7], non_blocking=True)
+                ei.record()
+        outs = []
+        for xd, ei, eo, st, cfg in api_calls:
+            comp.wait_event(ei)
+            outs.append(mbp.kernel_fn({"x": xd, "config": cfg}, st))
+            eo.record()
+        with torch.cuda.stream(d2h_s):
+            for c, o, (_, _, eo, _, _) in zip(calls, outs, api_calls):
+                d2h_s.wait_event(eo)
+                c[8].copy_(o, non_blocking=True)
         comp.wait_stream(d2h_s)
 
     for _ in range(max(1, args.warmup)):
@@ -584,6 +592,15 @@ def run_mbp(args, rank, world):
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     del g_api
     e2e_ok = all(torch.equal(c[8], c[6].cpu()) for c in calls)  # the host copies hold the step's outputs
+    # host cost of one kernel_fn call (checks, output allocation, geometry / tensor-map caches, launch), issued
+    # back to back on device-resident inputs: the CPU time per call, not a device time
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(8):
+        for xd, _, _, st, cfg in api_calls:
+            mbp.kernel_fn({"x": xd, "config": cfg}, st)
+    host_us_call = (time.perf_counter() - t0) * 1e6 / (8 * len(api_calls))
+    torch.cuda.synchronize()
     h2d = sum(2 * c[3] * c[4].k for c in calls)
     d2h = sum(2 * c[3] * c[4].n for c in calls)
 
@@ -617,7 +634,8 @@ def run_mbp(args, rank, world):
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
                     "timing": "CUDA-graph replay of the public-API step (per call: H2D of x on a copy stream, "
                               "kernel_fn, D2H of out on a second copy stream, overlapping the other calls)",
-                    "eager_ms_per_step": round(eager_ms, 4), "outputs_match_device": e2e_ok},
+                    "eager_ms_per_step": round(eager_ms, 4), "host_us_per_kernel_fn_call": round(host_us_call, 2),
+                    "outputs_match_device": e2e_ok},
             "gpu_launches": len(calls) * args.steps,
             "clocks": clocks,
             "parity": parity,
@@ -737,9 +755,11 @@ def run_mbp_tp(args, rank, world):
     config5 = {}
     for layer in ("qkv_gate", "o"):
         lin, w, p = lins[(layer, "plain")], weights[(layer, "plain")], full[(layer, "plain")]
+        dt = torch.bfloat16 if layer == "qkv_gate" else torch.float32  # the shard's own output (no exchange)
         for m in TP_MS:
             x = make_x(m, p.k, dev)
-            us = torch.tensor([time_after_flush(lambda: lin(x), flush)], device=dev)
+            us = torch.tensor([time_after_flush(lambda: lin(x), flush),
+                               time_after_flush(lambda: lin._local(x, dt), flush)], device=dev)
             dist.all_reduce(us, op=dist.ReduceOp.MAX)
             o = lin(x)
             ok1, err = close_check(o, x.float() @ w.float().T)
@@ -747,7 +767,8 @@ def run_mbp_tp(args, rank, world):
             diff_unsharded = max(diff_unsharded, float((o.float() - single.float()).abs().max()))
             par_ok &= ok1
             par_err = max(par_err, err)
-            config5[f"{layer}_m{m}"] = {"us": round(float(us.item()), 2), "parity": "ok" if ok1 else "FAIL",
+            config5[f"{layer}_m{m}"] = {"us": round(float(us[0]), 2), "shard_kernel_us": round(float(us[1]), 2),
+                                        "parity": "ok" if ok1 else "FAIL",
                                         "path": ("GEMV + " + ("peer-store exchange" if transport == "p2p"
                                                               else "NCCL")) if m <= mbp.GEMV_MAX_M
                                         else "tcgen05 GEMM + NCCL " + ("all-gather" if layer == "qkv_gate"
@@ -772,22 +793,27 @@ def run_mbp_tp(args, rank, world):
     hx = [c[2].cpu().pin_memory() for c in calls]
     ho = [torch.empty((c[4], c[5]), dtype=torch.bfloat16).pin_memory() for c in calls]
     h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
+    x_in = [torch.empty_like(c[2]) for c in calls]
+    ev_in = [torch.cuda.Event() for _ in calls]
+    ev_out = [torch.cuda.Event() for _ in calls]
 
     def api_step():
         comp = torch.cuda.current_stream()
-        h2d_s.wait_stream(comp)
+        h2d_s.wait_stream(comp)  # the previous step's kernels have read the input buffers
         d2h_s.wait_stream(comp)
-        for c, xh, oh in zip(calls, hx, ho):
-            with torch.cuda.stream(h2d_s):
-                xd = xh.to(dev, non_blocking=True)
-            comp.wait_stream(h2d_s)
-            xd.record_stream(comp)
-            out = c[1](xd)
-            d2h_s.wait_stream(comp)
-            with torch.cuda.stream(d2h_s):
-                oh.copy_(out, non_blocking=True)
-            out.record_stream(d2h_s)
-        comp.wait_stream(h2d_s)
+        with torch.cuda.stream(h2d_s):
+            for xd, xh, ei in zip(x_in, hx, ev_in):
+                xd.copy_(xh, non_blocking=True)
+                ei.record()
+        outs = []
+        for c, xd, ei, eo in zip(calls, x_in, ev_in, ev_out):
+            comp.wait_event(ei)
+            outs.append(c[1](xd))
+            eo.record()
+        with torch.cuda.stream(d2h_s):
+            for o, oh, eo in zip(outs, ho, ev_out):
+                d2h_s.wait_event(eo)
+                oh.copy_(o, non_blocking=True)
         comp.wait_stream(d2h_s)
 
     def timed_max(run, n):

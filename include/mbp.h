@@ -229,6 +229,16 @@ int mbp_gemv_c12_tp(const mbp_c12* w, const uint16_t* x, int ldx, int m, const m
  * S:5424, rwdl S:5377): out_f32[m, n] = x . hi^T + x . lo^T, FP32 accumulation. ---- */
 int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, const mbp_gemv_geom* geom,
                     cudaStream_t stream);
+/* The same product on the tcgen05 tensor cores (replaces the wide-router family rwdl_128 / rwdl_256, S:5377):
+ * A = the hi and lo units in TMEM, two MMAs per K step into one FP32 accumulator, the K range split over a
+ * thread-block cluster (<= 16) reduced in a fixed order through distributed shared memory.  bn = token tile
+ * (multiple of 16, <= 128; 0 = default), split = cluster size (<= 16, and >= k / 2048 so that no CTA accumulates
+ * more than 2048 columns on the tensor pipe, which keeps the 1e-5 accuracy; 0 = choose); k <= MBP_ROUTER_TC_MAX_K.
+ * mbp_router_hilo takes this path when geom is NULL, m >= MBP_ROUTER_TC_MIN_M and k <= MBP_ROUTER_TC_MAX_K. ---- */
+#define MBP_ROUTER_TC_MIN_M 257 /* measured: the GEMV is faster up to 256 tokens, this path from 384 */
+#define MBP_ROUTER_TC_MAX_K 32768
+int mbp_router_hilo_tc(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, int bn, int split,
+                       cudaStream_t stream);
 
 /* ---- Router consumer (no counterpart in the reference, which stops at the logits): the k largest of each
  * token's e logits (rows ld floats apart; e <= 1024, k <= min(e, 32)), ids[t][j] in descending logit order (equal

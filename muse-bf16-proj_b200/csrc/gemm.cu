@@ -6,21 +6,25 @@
 // (S:2309-2376, out of scope), which read unpacked BF16 weights; here the weights stay packed in HBM.
 //
 // CTA tile: 128 weight rows (8 row tiles) x BN tokens (<= 256) x a K range; `split` CTAs of a cluster share
-// one tile's K range and reduce through distributed shared memory.  Warp roles:
-//   warp 0       TMA producer of the weights: per 64-column chunk, one 3-D box of 8 packed units (12 KB);
-//   warp 18      TMA producer of x: per chunk one 2-D box of the x tile (BN rows x 128 bytes, 128-byte
-//                swizzle); the two rings run independently, so an x stage is refilled as soon as its MMA is done;
-//   warp 19      MMA scheduler: waits for each chunk's A and x stages and hands the chunk to the issuer on a
-//                named barrier, so the issuing thread never polls an mbarrier behind its own MMAs;
+// one tile's K range and reduce through distributed shared memory.  The K range advances in stages of two
+// 64-column sub-tiles: two consecutive chunks of the 12-bit weights, or one chunk's hi and lo tiles of the FP32
+// router (both multiplied by the same x tile into the same accumulator).  Warp roles:
+//   warp 0       TMA producer of the weights: per stage one 3-D box of 8 row tiles x 2 sub-tiles;
+//   warp 18      TMA producer of x: per stage the stage's x tiles (BN rows x 128 bytes each, 128-byte swizzle);
+//                the two rings run independently, so an x stage is refilled as soon as its MMAs are done;
+//   warp 19      MMA scheduler: waits for each stage's A and x and hands the stage to the issuer on a named
+//                barrier, so the issuing thread never polls an mbarrier behind its own MMAs;
 //   warp 1       allocates TMEM (the accumulator, then the decoded-A ring); lane 0 issues tcgen05.mma (M=128,
-//                N=BN, K=16, BF16 -> FP32) x4 per chunk, A from TMEM and B = x from a K-major SW128 shared-memory
-//                descriptor; tcgen05.commit frees the A and x stages and finally signals the accumulator;
-//   warps 2-17   decoders in kGroups groups of 8 warps; group g handles every kGroups-th chunk, each warp decodes
-//                one row tile in registers (same decode and escape cursor as the GEMV), transposes its K pairs
-//                across its lane quads and writes the tile with tcgen05.st straight into TMEM as the MMA's A
-//                operand: the decoded weights never pass through shared memory, whose bandwidth (TMA writes and
-//                the MMA's operand reads) otherwise bounds the 256-token tiles.  Afterwards they read the
-//                accumulator (tcgen05.ld 32x32b) and store (or cluster-reduce) it.
+//                N=BN, K=16, BF16 -> FP32) x8 per stage, A from TMEM and B = x from a K-major SW128 shared-memory
+//                descriptor; tcgen05.commit frees the A and x stages and finally signals the accumulator.  Two
+//                sub-tiles per stage halve the commits and hand-overs per MMA, the issue gap that bounds the
+//                one-chunk stages (the tensor pipe drained while they ran);
+//   warps 2-17   decoders, one per (row tile, sub-tile) of every stage: each decodes its unit in registers (same
+//                decode and escape cursor as the GEMV; the hi/lo units are copied as they are), transposes its K
+//                pairs across its lane quads and writes the tile with tcgen05.st straight into TMEM as the
+//                MMA's A operand: the decoded weights never pass through shared memory, whose bandwidth (TMA
+//                writes and the MMA's operand reads) otherwise bounds the 256-token tiles.  Afterwards they read
+//                the accumulator (tcgen05.ld 32x32b) and store (or cluster-reduce) it.
 // All waits are bounded; TMEM is always released.
 #include "common.cuh"
 #include "escape.cuh"
@@ -35,26 +39,36 @@ using namespace mbp;
 
 namespace {
 
-constexpr int kGroups = 2;                 // decoder groups working on alternate chunks
-constexpr int kDecWarps = 8 * kGroups;
+constexpr int kDecWarps = 16;              // 8 row tiles x 2 sub-tiles per stage
 constexpr int kXWarp = 2 + kDecWarps;      // the x producer
-constexpr int kSchedWarp = 3 + kDecWarps;  // waits for each chunk's operands on behalf of the MMA issuer
+constexpr int kSchedWarp = 3 + kDecWarps;  // waits for each stage's operands on behalf of the MMA issuer
 constexpr int kThreads = 32 * (4 + kDecWarps);
 constexpr int kHandBar = 1;                // named barrier of the scheduler -> issuer hand-over (64 threads)
-constexpr int kPS = 6;                     // packed ring depth
-constexpr int kAS = 2;                     // decoded-A ring depth
-constexpr int kXS = 4;                     // x ring depth
-// Decoder group g owns chunks i = g (mod kGroups).  A ring whose barriers the decoders wait on must give every
-// stage to a single group (depth a multiple of kGroups): otherwise a group could wait for use k+1 of a stage
-// while use k, owned by the other group and completed out of order by the TMA engine, is still pending, and
-// mbarrier parity waits, which only tell the current phase from the previous one, would return on the stale
-// phase (wrong data, and arrivals counted into the wrong phase).
-static_assert(kPS % kGroups == 0 && kAS % kGroups == 0, "ring depths must be multiples of the decoder groups");
-constexpr int kPackedStage = 8 * MBP_C12_UNIT_BYTES;  // 12 KB
+constexpr int kAS = 2;                     // decoded-A ring depth (stages of 64 TMEM columns)
+constexpr int kXS = 2;                     // x ring depth (stages)
 constexpr int kMaxSmem = 227 * 1024;
+constexpr int kRouterTcMaxChunks = 32;     // most 64-column chunks one CTA accumulates in the FP32 router
+
+// The two weight formats.  A row tile's sub-tile is one 12-bit unit (1.5 KB, decoded in registers; a stage holds
+// two consecutive chunks, each with its own x tile) or, for the FP32 router, one BF16 hi or lo unit (2 KB,
+// copied as it is: the packer already writes it in the decoder's register layout; a stage is one chunk).
+template <bool HILO>
+struct WFmt;
+template <>
+struct WFmt<false> {
+  static constexpr int kSub = MBP_C12_UNIT_BYTES;  // bytes of one row tile's sub-tile
+  static constexpr int kPS = 3;                    // packed ring depth (stages)
+  static constexpr int kXTiles = 2;                // x tiles per stage
+};
+template <>
+struct WFmt<true> {
+  static constexpr int kSub = MBP_RAW_UNIT_BYTES;
+  static constexpr int kPS = 4;
+  static constexpr int kXTiles = 1;
+};
 
 struct __align__(64) GemmParams {
-  CUtensorMap wmap;  // units as [R][C][192 x u64], box {192, 1, 8}
+  CUtensorMap wmap;  // units as [R][C][192 x u64], box {192, 2, 8}; hi/lo units as [R][2C][256 x u64], box {256, 2, 8}
   CUtensorMap xmap;  // x [m, k] bf16, box {64 columns, BN rows}, 128-byte swizzle
   const uint8_t* units;
   const uint8_t* bases;
@@ -63,6 +77,7 @@ struct __align__(64) GemmParams {
   void* out;
   int C, Rout, m, ldo, bn, split;
   int f32out;
+  int wsubs;                   // sub-tiles per weight box: 2 (1 for a 12-bit matrix of a single chunk)
   unsigned long long wait_ns;  // limit of every bounded wait
 };
 
@@ -70,14 +85,17 @@ struct GLayout {
   int packed, a, x, xr, bars, tmem_slot, total;
 };
 
-__host__ __device__ inline GLayout gemm_layout(int bn) {
+__host__ __device__ inline GLayout gemm_layout(int bn, bool hilo) {
+  const int ps = hilo ? WFmt<true>::kPS : WFmt<false>::kPS;
+  const int stage = 16 * (hilo ? WFmt<true>::kSub : WFmt<false>::kSub);
+  const int xt = hilo ? WFmt<true>::kXTiles : WFmt<false>::kXTiles;
   GLayout L;
   L.packed = 0;
-  L.a = L.packed + kPS * kPackedStage;  // (no shared-memory A: the decoded tiles live in TMEM)
-  L.x = L.a;                            // multiple of 1024
-  L.xr = L.x + kXS * bn * 128;          // bn multiple of 16 -> multiple of 2048
+  L.a = L.packed + ps * stage;  // (no shared-memory A: the decoded tiles live in TMEM)
+  L.x = L.a;                    // multiple of 1024
+  L.xr = L.x + kXS * xt * bn * 128;  // bn multiple of 16 -> multiple of 2048
   L.bars = L.xr + kDecWarps * kMaskUnitBytes;
-  L.tmem_slot = L.bars + 8 * (2 * kPS + 2 * kAS + 2 * kXS + 1);
+  L.tmem_slot = L.bars + 8 * (2 * ps + 2 * kAS + 2 * kXS + 1);
   L.total = L.tmem_slot + 16;
   return L;
 }
@@ -191,12 +209,15 @@ MBP_DEV void store_elem(const GemmParams& p, int tok, int row, float f) {
     reinterpret_cast<uint16_t*>(p.out)[(size_t)tok * p.ldo + row] = __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 
+template <bool HILO>
 __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ GemmParams p) {
+  using W = WFmt<HILO>;
+  constexpr int kPS = W::kPS, kSub = W::kSub, kStage = 16 * W::kSub;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* sm = smem_raw + (base - raw);
-  const GLayout L = gemm_layout(p.bn);
+  const GLayout L = gemm_layout(p.bn, HILO);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t bars = base + L.bars;
   const uint32_t pfull = bars, pempty = pfull + 8 * kPS;
@@ -210,19 +231,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   const int tok0 = blockIdx.y * p.bn;
   const int ks = blockIdx.z;       // K split index == cluster rank (cluster dims 1 x 1 x split)
   const int cs = (int)((long long)ks * C / p.split), ce = (int)((long long)(ks + 1) * C / p.split);
-  const int nc = ce - cs;
-  // TMEM: the accumulator (acc_cols >= bn columns), then the decoded-A ring (kAS x 32 columns)
+  const int nc = ce - cs;                        // chunks of this CTA
+  const int nst = HILO ? nc : (nc + 1) / 2;      // stages (the last 12-bit stage may hold one chunk)
+  const int xbytes = p.bn * 128;                 // one x tile
+  // TMEM: the accumulator (acc_cols >= bn columns), then the decoded-A ring (kAS x 64 columns)
   const uint32_t acc_cols = p.bn <= 32 ? 32 : p.bn <= 64 ? 64 : p.bn <= 128 ? 128 : 256;
   uint32_t tmem_cols = 32;
-  while (tmem_cols < acc_cols + 32 * kAS) tmem_cols *= 2;
+  while (tmem_cols < acc_cols + 64 * kAS) tmem_cols *= 2;
   const uint32_t a_col0 = acc_cols;
 
   // Programmatic dependent launch: the packed weights never depend on the previous kernel of the stream, so the
   // first ring's units are pulled into L2 while it drains; every thread waits for it before touching x or out.
   if (warp == 0 && lane < 8 * kPS) {
     const int d = lane & 7, i = lane >> 3;
-    if (rb0 + d < p.Rout && i < nc)
-      prefetch_l2(p.units + ((size_t)(rb0 + d) * C + cs + i) * MBP_C12_UNIT_BYTES, MBP_C12_UNIT_BYTES);
+    if (rb0 + d < p.Rout && i < nst) {
+      const size_t unit = HILO ? (size_t)(rb0 + d) * C + cs + i : (size_t)(rb0 + d) * C + cs + 2 * i;
+      const int subs = HILO ? 2 : (2 * i + 1 < nc ? 2 : 1);  // stays inside this CTA's chunks
+      prefetch_l2(p.units + unit * (HILO ? 2 * kSub : kSub), subs * kSub);
+    }
   }
   grid_dep_wait();
   grid_dep_launch();
@@ -230,10 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   if (tid == 0) {
     for (int i = 0; i < kPS; ++i) {
       mbar_init(pfull + 8 * i, 1);
-      mbar_init(pempty + 8 * i, 8 * 32);
+      mbar_init(pempty + 8 * i, kDecWarps * 32);
     }
     for (int i = 0; i < kAS; ++i) {
-      mbar_init(afull + 8 * i, 8 * 32);
+      mbar_init(afull + 8 * i, kDecWarps * 32);
       mbar_init(aempty + 8 * i, 1);
     }
     for (int i = 0; i < kXS; ++i) {
@@ -259,34 +285,40 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
 
   if (warp == 0) {
     // ---------------- weight producer ----------------
+    // One box per stage: 8 row tiles x 2 sub-tiles.  A last 12-bit stage with one chunk still loads two (the
+    // second belongs to the next K range, or lies past the matrix and is zero-filled); its MMAs are skipped.
     if (lane == 0) {
-      for (int i = 0; i < nc; ++i) {
+      for (int i = 0; i < nst; ++i) {
         const int ps = i % kPS;
         if (i >= kPS && !mbar_wait(pempty + 8 * ps, ((i / kPS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
-        mbar_arrive_expect_tx(pfull + 8 * ps, kPackedStage);
-        tma_load_3d(base + L.packed + ps * kPackedStage, &p.wmap, 0, cs + i, rb0, pfull + 8 * ps);
+        mbar_arrive_expect_tx(pfull + 8 * ps, (uint32_t)(p.wsubs * 8 * kSub));
+        tma_load_3d(base + L.packed + ps * kStage, &p.wmap, 0, HILO ? 2 * (cs + i) : cs + 2 * i, rb0,
+                    pfull + 8 * ps);
       }
     }
     __syncwarp();  // lanes 1-31 wait here for the producing lane
   } else if (warp == kXWarp) {
     // ---------------- x producer ----------------
     if (lane == 0) {
-      for (int i = 0; i < nc; ++i) {
+      for (int i = 0; i < nst; ++i) {
         const int xs = i % kXS;
+        const int nt = HILO ? 1 : min(2, nc - 2 * i);
         if (i >= kXS && !mbar_wait(xempty + 8 * xs, ((i / kXS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
-        mbar_arrive_expect_tx(xfull + 8 * xs, (uint32_t)p.bn * 128);
-        tma_load_2d(base + L.x + xs * p.bn * 128, &p.xmap, (cs + i) * 64, tok0, xfull + 8 * xs);
+        mbar_arrive_expect_tx(xfull + 8 * xs, (uint32_t)(nt * xbytes));
+        for (int t = 0; t < nt; ++t)
+          tma_load_2d(base + L.x + (xs * W::kXTiles + t) * xbytes, &p.xmap, (HILO ? cs + i : cs + 2 * i + t) * 64,
+                      tok0, xfull + 8 * xs);
       }
     }
     __syncwarp();
   } else if (warp == kSchedWarp) {
     // ---------------- MMA scheduler ----------------
-    // Waits for chunk i's A and x stages while the issuer is still feeding chunk i-1 to the tensor pipe, then
-    // meets it on a named barrier.  (An mbarrier wait in the issuing thread itself, right behind its MMAs and
-    // commits, measured ~300-450 cycles per chunk even on phases completed long before.)  Every round is
-    // always met, so a timed-out wait ends both warps' loops through the abort word instead of a missing partner.
+    // Waits for stage i's A and x while the issuer is still feeding stage i-1 to the tensor pipe, then meets it
+    // on a named barrier.  (An mbarrier wait in the issuing thread itself, right behind its MMAs and commits,
+    // measured ~300-450 cycles per wait even on phases completed long before.)  Every round is always met, so a
+    // timed-out wait ends both warps' loops through the abort word instead of a missing partner.
     bool ok = true;
-    for (int i = 0; i < nc; ++i) {
+    for (int i = 0; i < nst; ++i) {
       if (lane == 0 && ok) {
         ok = mbar_wait(afull + 8 * (i % kAS), (i / kAS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns) &&
              mbar_wait(xfull + 8 * (i % kXS), (i / kXS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns);
@@ -300,15 +332,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     // descriptors of the first stages; the 14-bit start-address field (bytes >> 4) of a descriptor advances by
     // offset >> 4 without carrying out (shared addresses stay below 256 KB)
     const uint64_t db0 = smem_desc_sw128(base + L.x);
-    for (int i = 0; i < nc; ++i) {
-      named_bar_sync(kHandBar, 64);  // the scheduler saw chunk i's stages full
+    for (int i = 0; i < nst; ++i) {
+      named_bar_sync(kHandBar, 64);  // the scheduler saw stage i's A and x full
       if (lane == 0 && *abort_word == 0u) {
         const int as = i % kAS, xs = i % kXS;
         tc_fence_after();
-        const uint32_t ta = tmem + a_col0 + (uint32_t)as * 32u;
-        const uint64_t db = db0 + (uint64_t)((xs * p.bn * 128) >> 4);
+        const uint32_t ta = tmem + a_col0 + (uint32_t)(as * 64);
+        const uint64_t db = db0 + (uint64_t)((xs * W::kXTiles * xbytes) >> 4);
 #pragma unroll
         for (int k = 0; k < 4; ++k) tc_mma_ts(tmem, ta + 8 * k, db + 2 * k, idesc, (i | k) != 0);
+        if (HILO || 2 * i + 1 < nc) {
+          // second sub-tile: the lo tile against the same x, or the next chunk against its own x tile
+          const uint64_t db1 = HILO ? db : db + (uint64_t)(xbytes >> 4);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) tc_mma_ts(tmem, ta + 32 + 8 * k, db1 + 2 * k, idesc, 1u);
+        }
         tc_commit(aempty + 8 * as);
         tc_commit(xempty + 8 * xs);
       }
@@ -317,50 +355,65 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
     if (lane == 0) tc_commit(done);  // fires when every issued MMA has completed
     __syncwarp();
   } else {
-    // ---------------- decoders: group gi takes local chunks gi, gi + kGroups, ... ----------------
-    // Row tile d of the 128-row tile.  A warp may only write its TMEM lane quadrant (warp % 4), so row tile d
-    // (lanes 16d .. 16d+15) goes to a warp of quadrant d / 2: the warps of a group cover quadrants 2, 3, 0, 1 twice.
-    const int dw = warp - 2, gi = dw >> 3, di = dw & 7;
-    const int d = 2 * ((di + 2) & 3) + (di >> 2);
+    // ---------------- decoders: warp (d, j) = row tile d, sub-tile j of every stage ----------------
+    // A warp may only write its TMEM lane quadrant (warp % 4), so row tile d (lanes 16d .. 16d+15) goes to a warp
+    // of quadrant d / 2: the four warps of quadrant q take (2q, 0), (2q + 1, 0), (2q, 1), (2q + 1, 1).
+    const int dw = warp - 2, q = (dw + 2) & 3, qi = dw >> 2;
+    const int d = 2 * q + (qi & 1), j = qi >> 1;
+    const int t = lane & 3;
+    const uint32_t ta0 = tmem + ((uint32_t)(16 * d) << 16) + a_col0 + 32u * (uint32_t)j;
     const int rt = rb0 + d;
     const bool valid = rt < p.Rout;
     uint32_t T0 = 0, T1 = 0;
     EscCursor cur;
     const uint32_t xr = base + L.xr + dw * kMaskUnitBytes;
-    mask_clear(xr, kMaskUnitBytes, lane);
-    if (valid) {
-      const uint32_t b = p.bases[rt];
-      T0 = table_lo(b);
-      T1 = table_hi(b);
-      cur.init(p.esc, p.esc_off[(size_t)rt * C + cs], p.esc_off[(size_t)rt * C + ce], lane);
-    } else {
-      cur.init(p.esc, 0, 0, lane);
-    }
-    const int t = lane & 3;
-    for (int i = gi; i < nc; i += kGroups) {
-      const int ps = i % kPS, as = i % kAS;
-      if (!mbar_wait(pfull + 8 * ps, (i / kPS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns)) break;
-      const unsigned char* u = sm + L.packed + ps * kPackedStage + d * MBP_C12_UNIT_BYTES + lane * 16;
-      const uint4 p0 = *reinterpret_cast<const uint4*>(u);
-      const uint4 p1 = *reinterpret_cast<const uint4*>(u + 512);
-      const uint4 p2 = *reinterpret_cast<const uint4*>(u + 1024);
-      uint32_t A[16];
-      const uint32_t c = (uint32_t)(cs + i);
-      if (valid) cur.seek(c, lane);
-      if (valid && cur.next_chunk == c) {
-        uint32_t tgt[1] = {0u};
-        cur.scatter<1>(c, c + 1, xr, kMaskUnitBytes, lane, tgt);
-        __syncwarp();
-        uint4 m0, m1;
-        take_mask(xr, tgt[0], lane, m0, m1);
-        decode_unit_m(p0, p1, p2, T0, T1, m0, m1, A);
+    if constexpr (!HILO) {
+      mask_clear(xr, kMaskUnitBytes, lane);
+      if (valid) {
+        const uint32_t b = p.bases[rt];
+        T0 = table_lo(b);
+        T1 = table_hi(b);
+        cur.init(p.esc, p.esc_off[(size_t)rt * C + cs], p.esc_off[(size_t)rt * C + ce], lane);
       } else {
-        decode_unit(p0, p1, p2, T0, T1, A);
+        cur.init(p.esc, 0, 0, lane);
       }
-      // A[0] depends on p0 and p2, A[8] on p1: all three loads have returned before the stage is handed back
-      mbar_arrive_dep(pempty + 8 * ps, A[0] ^ A[8]);
+    }
+    for (int i = 0; i < nst; ++i) {
+      const int ps = i % kPS, as = i % kAS;
+      const bool live = HILO || 2 * i + j < nc;  // a last 12-bit stage with one chunk has no sub-tile 1
+      if (!mbar_wait(pfull + 8 * ps, (i / kPS) & 1, MBP_DEV_TIMEOUT_FULL, p.wait_ns)) break;
+      const unsigned char* u = sm + L.packed + ps * kStage + (p.wsubs * d + j) * kSub + lane * 16;
+      uint32_t A[16];
+      uint32_t dep = 0;
+      if constexpr (HILO) {
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          const uint4 v = *reinterpret_cast<const uint4*>(u + qq * 512);
+          A[4 * qq] = v.x, A[4 * qq + 1] = v.y, A[4 * qq + 2] = v.z, A[4 * qq + 3] = v.w;
+        }
+        dep = A[0] ^ A[4] ^ A[8] ^ A[12];  // a value from each load
+      } else if (live) {
+        const uint4 p0 = *reinterpret_cast<const uint4*>(u);
+        const uint4 p1 = *reinterpret_cast<const uint4*>(u + 512);
+        const uint4 p2 = *reinterpret_cast<const uint4*>(u + 1024);
+        const uint32_t c = (uint32_t)(cs + 2 * i + j);
+        if (valid) cur.seek(c, lane);
+        if (valid && cur.next_chunk == c) {
+          uint32_t tgt[1] = {0u};
+          cur.scatter<1>(c, c + 1, xr, kMaskUnitBytes, lane, tgt);
+          __syncwarp();
+          uint4 m0, m1;
+          take_mask(xr, tgt[0], lane, m0, m1);
+          decode_unit_m(p0, p1, p2, T0, T1, m0, m1, A);
+        } else {
+          decode_unit(p0, p1, p2, T0, T1, A);
+        }
+        dep = A[0] ^ A[8];  // A[0] depends on p0 and p2, A[8] on p1
+      }
+      // every load of the stage has returned before it is handed back
+      mbar_arrive_dep(pempty + 8 * ps, dep);
       if (i >= kAS && !mbar_wait(aempty + 8 * as, ((i / kAS) & 1) ^ 1, MBP_DEV_TIMEOUT_EMPTY, p.wait_ns)) break;
-      tc_st_a(tmem + ((uint32_t)(16 * d) << 16) + a_col0 + (uint32_t)as * 32u, A, t);
+      if (live) tc_st_a(ta0 + (uint32_t)(as * 64), A, t);
       tc_fence_before();  // the stores are complete (wait::st) and ordered before the arrive
       mbar_arrive(afull + 8 * as);
     }
@@ -435,43 +488,53 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   }
 }
 
-// units [R][C][1536 bytes] viewed as a 3-D tensor of u64: {192, C, R}, box {192, 1, 8}
-bool encode_units_3d(CUtensorMap* map, const void* units, int R, int C) {
+// Weight units as a 3-D tensor of u64 with a box of 8 row tiles x 2 sub-tiles per stage:
+//   12-bit units [R][C][1536 bytes] -> {192, C, R}, box {192, 2, 8} (chunks c, c + 1; {192, 1, 8} for a matrix of
+//   one chunk);
+//   hi/lo units  [R][C][2][2048 bytes] -> {256, 2C, R}, box {256, 2, 8} (chunk c = indices 2c, 2c + 1).
+// (Measured alternative: 128-byte rows with a 128-byte swizzle and a ring as deep as shared memory allows was
+// 10-15 % slower; the decoders' instruction issue, not the copy engine, bounds the small-M calls.)
+bool encode_units_3d(CUtensorMap* map, const void* units, int R, int C, bool hilo) {
   auto fn = encode_fn();
   if (!fn) return false;
-  const cuuint64_t dims[3] = {192, (cuuint64_t)C, (cuuint64_t)R};
-  const cuuint64_t strides[2] = {(cuuint64_t)MBP_C12_UNIT_BYTES, (cuuint64_t)C * MBP_C12_UNIT_BYTES};
-  const cuuint32_t box[3] = {192, 1, 8};
+  const cuuint64_t inner = hilo ? 256 : 192, mid = hilo ? 2 * (cuuint64_t)C : (cuuint64_t)C;
+  const cuuint64_t row = (cuuint64_t)C * (hilo ? 2 * MBP_RAW_UNIT_BYTES : MBP_C12_UNIT_BYTES);
+  const cuuint64_t dims[3] = {inner, mid, (cuuint64_t)R};
+  const cuuint64_t strides[2] = {inner * 8, row};
+  const cuuint32_t box[3] = {(cuuint32_t)inner, mid >= 2 ? 2u : 1u, 8};
   const cuuint32_t estr[3] = {1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(units), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-std::mutex g_mu;
-std::map<int, bool> g_attr_done;
-std::map<std::tuple<int, int, int>, int> g_clusters;  // (device, split, smem) -> co-resident clusters
+using GemmKernel = void (*)(GemmParams);
 
-int ensure_attr() {
+GemmKernel kernel_of(bool hilo) { return hilo ? k_gemm<true> : k_gemm<false>; }
+
+std::mutex g_mu;
+std::map<std::pair<int, bool>, bool> g_attr_done;
+std::map<std::tuple<int, bool, int, int>, int> g_clusters;  // (device, format, split, smem) -> co-resident CTAs
+
+int ensure_attr(bool hilo) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return MBP_ERR_LAUNCH;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_attr_done.count(dev)) return MBP_OK;
-  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_gemm), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kMaxSmem) != cudaSuccess)
+  if (g_attr_done.count({dev, hilo})) return MBP_OK;
+  const void* fn = reinterpret_cast<const void*>(kernel_of(hilo));
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem) != cudaSuccess)
     return MBP_ERR_SMEM;
-  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_gemm), cudaFuncAttributeNonPortableClusterSizeAllowed,
-                           1) != cudaSuccess)
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
     return MBP_ERR_CLUSTER;
-  g_attr_done[dev] = true;
+  g_attr_done[{dev, hilo}] = true;
   return MBP_OK;
 }
 
-int co_resident_ctas(int split, int smem) {
+int co_resident_ctas(bool hilo, int split, int smem) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const auto key = std::make_tuple(dev, split, smem);
+  const auto key = std::make_tuple(dev, hilo, split, smem);
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_clusters.find(key);
@@ -491,7 +554,8 @@ int co_resident_ctas(int split, int smem) {
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    ctas = cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(&k_gemm), &cfg) == cudaSuccess
+    ctas = cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(kernel_of(hilo)), &cfg) ==
+                   cudaSuccess
                ? clusters * split
                : 0;
     cudaGetLastError();
@@ -501,76 +565,64 @@ int co_resident_ctas(int split, int smem) {
   return ctas;
 }
 
-// K split: the largest cluster (<= 8, >= 4 chunks per CTA) whose tiles still fit one wave of co-resident CTAs,
-// when the tile count alone leaves more than a quarter of the SMs idle.
-int choose_split(int tiles, int C, int smem) {
+// K split: the largest cluster (min_split .. max_split, >= 4 chunks per CTA) whose tiles still fit one wave of
+// co-resident CTAs, when the tile count alone leaves more than a quarter of the SMs idle; else min_split.
+int choose_split(bool hilo, int tiles, int C, int smem, int min_split, int max_split) {
   int sms = 148, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (tiles * 4 >= sms * 3) return 1;
-  int best = 1;
-  for (int s = 2; s <= 8; ++s) {
+  if (tiles * 4 >= sms * 3) return min_split;
+  int best = min_split;
+  for (int s = min_split < 2 ? 2 : min_split; s <= max_split; ++s) {
     if (C / s < 4) break;
-    const int cap = co_resident_ctas(s, smem);
+    const int cap = co_resident_ctas(hilo, s, smem);
     if (cap >= tiles * s && tiles * s <= sms) best = s;
   }
   return best;
 }
 
-int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out, int ldo, bool f32,
-                cudaStream_t stream) {
-  if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
-  if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
-  if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n || n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
-  if (m < 1) return MBP_ERR_M;
-  if (ldo < n_out) return MBP_ERR_SHAPE;
-  if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u)) return MBP_ERR_ALIGN;
-  // Token tile: all tokens up to 256.  Short K (<= 2048): a cluster split-K's reduction costs more than its
-  // short main loop saves, so smaller token tiles fill the SMs instead, down to 64 while one wave holds them
-  // (measured at M=256: o 8192x1024 11.5 us with 128-token tiles against 16.9 us with a 2-way K split).
-  int bn = m >= 256 ? 256 : ((m + 15) / 16) * 16;
-  if (w->k / 64 <= 32) {
-    int sms = 148, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int row_blocks = (n_out / 16 + 7) / 8;
-    int ntok = (m + bn - 1) / bn;
-    for (;;) {  // double the token tiles (balanced, multiples of 16 tokens) while they stay >= 64 and one wave
-      const int t2 = 2 * ntok, bn2 = ((m + t2 - 1) / t2 + 15) / 16 * 16;
-      if (bn2 < 64 || row_blocks * ((m + bn2 - 1) / bn2) > sms) break;
-      ntok = t2;
-      bn = bn2;
-    }
-  }
-  const GLayout L = gemm_layout(bn);
+int sm_count_here() {
+  int sms = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+// One launch of k_gemm<hilo>: units/bases/escapes describe the weights (bases and escapes unused for hi/lo),
+// R16 = row tiles of the weights, rout16 = row tiles written, C = 64-column chunks.  bn: token tile; split: K
+// split (cluster size; 0 = choose).
+int launch_gemm(bool hilo, const uint8_t* units, const uint8_t* bases, const int32_t* esc_off, const uint32_t* esc,
+                int R16, int rout16, int C, const uint16_t* x, int m, void* out, int ldo, bool f32, int bn, int split,
+                int min_split, int max_split, cudaStream_t stream) {
+  const GLayout L = gemm_layout(bn, hilo);
   const int smem = L.total + 1024;
   if (smem > kMaxSmem) return MBP_ERR_SMEM;
   // the cluster reduction reuses the ring area for a 128 x bn FP32 tile
   if (128 * ((bn + 31) / 32) * 32 * 4 > L.xr) return MBP_ERR_SMEM;
-  int rc = ensure_attr();
+  int rc = ensure_attr(hilo);
   if (rc) return rc;
   GemmParams p;
-  const int R = w->n / 16, C = w->k / 64;
-  const TmapKey wkey{w->units, (uint64_t)R, (uint64_t)C, 0, 0, 0, 0x200u};
-  if (!cached_map(&p.wmap, wkey, [&](CUtensorMap* mp) { return encode_units_3d(mp, w->units, R, C); }))
+  const TmapKey wkey{units, (uint64_t)R16, (uint64_t)C, 0, 0, 0, hilo ? 0x203u : 0x202u};
+  if (!cached_map(&p.wmap, wkey, [&](CUtensorMap* mp) { return encode_units_3d(mp, units, R16, C, hilo); }))
     return MBP_ERR_TMAP;
-  if (!encode_bf16_2d_cached(&p.xmap, x, (uint64_t)m, (uint64_t)w->k, (uint64_t)w->k, (uint32_t)bn, 64u,
+  if (!encode_bf16_2d_cached(&p.xmap, x, (uint64_t)m, (uint64_t)C * 64, (uint64_t)C * 64, (uint32_t)bn, 64u,
                              CU_TENSOR_MAP_SWIZZLE_128B))
     return MBP_ERR_TMAP;
-  p.units = w->units;
-  p.bases = w->bases;
-  p.esc_off = w->esc_off;
-  p.esc = w->esc;
+  p.units = units;
+  p.bases = bases;
+  p.esc_off = esc_off;
+  p.esc = esc;
   p.out = out;
   p.C = C;
-  p.Rout = n_out / 16;
+  p.Rout = rout16;
   p.m = m;
   p.ldo = ldo;
   p.bn = bn;
   p.f32out = f32 ? 1 : 0;
+  p.wsubs = (hilo || C >= 2) ? 2 : 1;
   p.wait_ns = wait_limit_ns();
   const int tiles = ((p.Rout + 7) / 8) * ((m + bn - 1) / bn);
-  p.split = choose_split(tiles, C, smem);
+  p.split = split > 0 ? split : choose_split(hilo, tiles, C, smem, min_split, max_split);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.Rout + 7) / 8, (m + bn - 1) / bn, p.split);
   cfg.blockDim = dim3(kThreads);
@@ -593,7 +645,34 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, k_gemm, p) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+  return cudaLaunchKernelEx(&cfg, kernel_of(hilo), p) == cudaSuccess ? MBP_OK : MBP_ERR_LAUNCH;
+}
+
+int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out, int ldo, bool f32,
+                cudaStream_t stream) {
+  if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
+  if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
+  if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n || n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
+  if (m < 1) return MBP_ERR_M;
+  if (ldo < n_out) return MBP_ERR_SHAPE;
+  if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u)) return MBP_ERR_ALIGN;
+  // Token tile: all tokens up to 256.  Short K (<= 2048): a cluster split-K's reduction costs more than its
+  // short main loop saves, so smaller token tiles fill the SMs instead, down to 64 while one wave holds them
+  // (measured at M=256: o 8192x1024 11.5 us with 128-token tiles against 16.9 us with a 2-way K split).
+  int bn = m >= 256 ? 256 : ((m + 15) / 16) * 16;
+  if (w->k / 64 <= 32) {
+    const int sms = sm_count_here();
+    const int row_blocks = (n_out / 16 + 7) / 8;
+    int ntok = (m + bn - 1) / bn;
+    for (;;) {  // double the token tiles (balanced, multiples of 16 tokens) while they stay >= 64 and one wave
+      const int t2 = 2 * ntok, bn2 = ((m + t2 - 1) / t2 + 15) / 16 * 16;
+      if (bn2 < 64 || row_blocks * ((m + bn2 - 1) / bn2) > sms) break;
+      ntok = t2;
+      bn = bn2;
+    }
+  }
+  return launch_gemm(false, w->units, w->bases, w->esc_off, w->esc, w->n / 16, n_out / 16, w->k / 64, x, m, out,
+                     ldo, f32, bn, 0, 1, 8, stream);
 }
 
 }  // namespace
@@ -608,6 +687,29 @@ int mbp_gemm_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t
 int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
                      cudaStream_t stream) {
   return gemm_launch(w, x, m, n_out, out, ldo, true, stream);
+}
+
+int mbp_router_hilo_tc(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, int bn, int split,
+                       cudaStream_t stream) {
+  if (!w || !w->units || !x || !out) return MBP_ERR_ARG;
+  const int C = w->k / 64;
+  if (w->n % 16 || w->k % 64 || C > kRouterTcMaxChunks * 16) return MBP_ERR_SHAPE;
+  if (m < 1) return MBP_ERR_M;
+  if (ldo < w->n) return MBP_ERR_SHAPE;
+  if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u)) return MBP_ERR_ALIGN;
+  // The tensor pipe's FP32 accumulation over one CTA's whole K range measured 1.4e-5 relative error against
+  // FP64 at 6144 columns (96 chunks, hi + lo), above the router's 1e-5 bound; with at most 32 chunks per CTA and
+  // the cluster's partial sums added in FP32 it stays well inside, so the K split never goes below that.
+  const int min_split = (C + kRouterTcMaxChunks - 1) / kRouterTcMaxChunks;
+  if (bn < 0 || bn > 128 || bn % 16 || split < 0 || split > 16 || split > C) return MBP_ERR_ARG;
+  if (split > 0 && split < min_split) return MBP_ERR_ARG;
+  if (bn == 0) {
+    // Token tiles of 64 (fewer when M is small), the K split filling the SMs through clusters of up to 16: the
+    // router has only two 128-row blocks, so its parallelism comes from the tokens and the K range.
+    bn = m >= 64 ? 64 : ((m + 15) / 16) * 16;
+  }
+  return launch_gemm(true, w->units, nullptr, nullptr, nullptr, w->n / 16, w->n / 16, C, x, m, out, ldo, true, bn,
+                     split, min_split, 16, stream);
 }
 
 }  // extern "C"

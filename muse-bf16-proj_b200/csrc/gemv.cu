@@ -1103,6 +1103,8 @@ int mbp_router_hilo(const mbp_hilo* w, const uint16_t* x, int m, float* out, int
   if (!w || !w->units || !x || !out) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766) return MBP_ERR_SHAPE;
   if (m < 1) return MBP_ERR_M;
+  if (!geom && m >= MBP_ROUTER_TC_MIN_M && w->k <= MBP_ROUTER_TC_MAX_K)
+    return mbp_router_hilo_tc(w, x, m, out, ldo, 0, 0, stream);
   mbp_gemv_geom g;
   if (!geom) {
     const int rc = plan_impl(FMT_HILO, w->n / 16, w->k / 64, m, true, ESC_NONE, &g);

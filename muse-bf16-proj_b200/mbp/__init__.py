@@ -21,12 +21,12 @@ import torch
 from . import ops, store
 from ._lib import MbpError, device_status, lib, set_wait_limit
 from .ops import (BASE_MATRIX, BASE_TILE, PackedC12, PackedHiLo, gemm, gemv, gemv_plan, pack_c12, pack_hilo,
-                  router, router_topk, unpack_c12)
+                  router, router_tc, router_topk, unpack_c12)
 from .store import load_packed, save_packed
 
 __all__ = ["Weights", "Config", "Inputs", "prepare", "kernel_fn", "MbpError", "PackedC12", "PackedHiLo", "pack_c12",
            "unpack_c12", "pack_hilo", "gemv", "gemm", "gemv_plan", "router", "device_status", "BASE_MATRIX", "BASE_TILE",
-           "save_packed", "load_packed", "store", "router_topk", "route", "set_wait_limit"]
+           "save_packed", "load_packed", "store", "router_topk", "route", "set_wait_limit", "router_tc"]
 
 LAYERS = ("qkv_gate", "o", "pooler", "unpooler", "router")
 GEMV_MAX_M = 32  # the reference's decode/verify boundary: small-M GEMVs up to 32 tokens (SM_MAX_M, S:252)

@@ -214,6 +214,21 @@ def router(p: PackedHiLo, x: torch.Tensor, out: torch.Tensor | None = None, geom
     return out
 
 
+def router_tc(p: PackedHiLo, x: torch.Tensor, out: torch.Tensor | None = None, bn: int = 0, split: int = 0):
+    """The router product on the tcgen05 tensor cores (``router`` takes this path above 256 tokens): token tile
+    ``bn`` (multiple of 16, <= 128) and K split over a cluster of ``split`` CTAs (<= 16, and at least k / 2048:
+    no CTA accumulates more than 2048 columns on the tensor pipe, which keeps the 1e-5 accuracy); 0 chooses."""
+    _check_x(x, p.k, p.units.device)
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty((m, p.n), dtype=torch.float32, device=x.device)
+    if out.dtype != torch.float32 or out.dim() != 2 or out.shape != (m, p.n) or out.stride(1) != 1:
+        raise ValueError("out must be a float32 [m, n] tensor with unit column stride")
+    check(lib().mbp_router_hilo_tc(ctypes.byref(p.desc), x.data_ptr(), m, out.data_ptr(), out.stride(0), bn, split,
+                                   _stream(x.device)), "mbp_router_hilo_tc")
+    return out
+
+
 def router_topk(logits: torch.Tensor, k: int, renorm: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
     """(weights f32 [m, k], ids int32 [m, k]): each row's k largest logits in descending order (equal logits:
     lower index first) and their softmax weights over the selection (renorm) or over the whole row."""

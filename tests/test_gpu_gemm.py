@@ -61,6 +61,23 @@ def test_gemm_token_counts(m):
     assert_close_bf16(out, ref_f32(x, w))
 
 
+@pytest.mark.parametrize("n,k,m", [(256, 64, 128), (256, 192, 64), (512, 320, 256), (1024, 7 * 64 * 9, 96),
+                                   (768, 64 * 37, 200)])
+def test_gemm_odd_chunk_counts(n, k, m):
+    """K ranges with an odd number of 64-column chunks (a last stage holding one chunk), down to a single chunk,
+    with and without a K split, on escape-bearing weights: within rtol 1e-4 / atol 1e-3 of the GEMV's FP32 output
+    (the same products summed in another order) and within the BF16 tolerance of the FP32 reference."""
+    import mbp
+    w = weight(n, k, seed=k, escape_frac=0.01)
+    p = mbp.pack_c12(w)
+    x = tokens(m, k, seed=m)
+    out = mbp.gemm(p, x, out_dtype=torch.float32)
+    ref = torch.cat([mbp.gemv(p, x[i:i + 32].contiguous(), out_dtype=torch.float32) for i in range(0, m, 32)])
+    assert torch.allclose(out, ref, rtol=1e-4, atol=1e-3)
+    assert_close_bf16(mbp.gemm(p, x), ref_f32(x, w))
+    assert mbp.device_status() == 0
+
+
 def test_gemm_partial_rows_and_f32():
     import mbp
     w = weight(8192, 1024, seed=5, escape_frac=0.01)

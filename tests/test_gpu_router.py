@@ -1,5 +1,7 @@
 """FP32 router through the BF16 hi/lo pair: within 1e-5 (relative, norm) of an FP64 reference (6144 -> 256
-experts), for M in {1, 8, 16, 32, 128, 256}, and one-hot exact against hi + lo (the reference's sm_exact, S:320-324)."""
+experts), for M in {1, 8, 16, 32, 128, 256}, and one-hot exact against hi + lo (the reference's sm_exact, S:320-324).
+The tensor-core path (M >= 64) is also checked at every token tile / cluster split it accepts, at the reference's
+own 8192-column router, on ragged token counts and expert counts, one-hot exact, and for identical bits on repeats."""
 import numpy as np
 import pytest
 import torch
@@ -43,6 +45,69 @@ def test_router_onehot_equals_hi_plus_lo():
         x[torch.arange(32), torch.arange(start, start + 32)] = 1.0
         out = mbp.router(p, x)
         assert torch.equal(out, exact[:, start:start + 32].T.contiguous())
+
+
+def _rel_fp64(out, x, w):
+    ref = oracle.linear_wf32_f64(bits_np(x), w.cpu().numpy())
+    got = out.double().cpu().numpy()
+    rows = np.linalg.norm(got - ref, axis=1) / np.linalg.norm(ref, axis=1)
+    return np.linalg.norm(got - ref) / np.linalg.norm(ref), rows.max()
+
+
+@pytest.mark.parametrize("m,k,n", [(64, 6144, 256), (100, 6144, 256), (128, 8192, 256), (256, 8192, 256),
+                                   (300, 6144, 256), (70, 1024, 96), (512, 2048, 128)])
+def test_router_tc_vs_fp64(m, k, n):
+    import mbp
+    w = router_weight(n, k, seed=m)
+    p = mbp.pack_hilo(w)
+    x = tokens(m, k, seed=m + 1)
+    for out in (mbp.router_tc(p, x), mbp.router(p, x)):  # the tensor-core path and the default route
+        rel, row = _rel_fp64(out, x, w)
+        assert rel <= 1e-5 and row <= 1e-5, (rel, row)
+    assert mbp.device_status() == 0
+
+
+@pytest.mark.parametrize("bn,split", [(16, 3), (32, 8), (64, 16), (64, 4), (128, 3), (128, 16), (48, 12)])
+def test_router_tc_geometries(bn, split):
+    import mbp
+    w = router_weight(256, 6144, seed=5)
+    p = mbp.pack_hilo(w)
+    x = tokens(256, 6144, seed=6)
+    out = mbp.router_tc(p, x, bn=bn, split=split)
+    rel, row = _rel_fp64(out, x, w)
+    assert rel <= 1e-5 and row <= 1e-5, (bn, split, rel, row)
+    again = mbp.router_tc(p, x, bn=bn, split=split)
+    assert torch.equal(out, again)  # fixed reduction order: identical bits
+    assert mbp.device_status() == 0
+
+
+def test_router_tc_onehot_equals_hi_plus_lo():
+    import mbp
+    w = router_weight(256, 1024, seed=4)
+    p = mbp.pack_hilo(w)
+    hi = w.to(torch.bfloat16)
+    lo = (w - hi.float()).to(torch.bfloat16)
+    exact = hi.float() + lo.float()
+    for start in range(0, 1024, 128):
+        x = torch.zeros(128, 1024, dtype=torch.bfloat16, device="cuda")
+        x[torch.arange(128), torch.arange(start, start + 128)] = 1.0
+        out = mbp.router_tc(p, x, split=4)
+        assert torch.equal(out, exact[:, start:start + 128].T.contiguous()), start
+
+
+def test_router_tc_rejects_bad_geometry():
+    import mbp
+    p = mbp.pack_hilo(router_weight(256, 1024))
+    x = tokens(64, 1024)
+    for bn, split in ((24, 0), (256, 0), (0, 17), (0, 32)):
+        with pytest.raises(mbp.MbpError):
+            mbp.router_tc(p, x, bn=bn, split=split)
+    # a cluster too small for the accuracy bound: at most 2048 columns per CTA (6144 -> split >= 3)
+    p = mbp.pack_hilo(router_weight(256, 6144))
+    x = tokens(64, 6144)
+    for bn, split in ((16, 1), (64, 2)):
+        with pytest.raises(mbp.MbpError):
+            mbp.router_tc(p, x, bn=bn, split=split)
 
 
 def test_router_through_api():
