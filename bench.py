@@ -54,7 +54,7 @@ MATS = (("qkv_gate", "plain"), ("o", "plain"), ("qkv_gate", "esc1pct"), ("o", "e
 VERIFY = {"qkv_gate": (14336, 6144), "o": (6144, 6144), "pooler": (1536, 6144), "unpooler": (6144, 1536)}
 VERIFY_MS = (128, 256)
 ROUTER_SHAPE = (256, 6144)
-ROUTER_MS = (1, 8, 16, 32, 128, 256)
+ROUTER_MS = (1, 8, 16, 32, 128, 256, 512)  # 512: past config 4, the tensor-core route
 CONFIG1_SHAPE = (4096, 4096)
 TP_MS = (1, 32, 256)
 TRAFFIC_FILE = os.path.join(ROOT, "profiles", "bench_step_traffic.md")
@@ -486,7 +486,8 @@ def run_mbp(args, rank, world):
         nbytes = pr.payload_bytes + 2 * m * pr.k + 4 * m * pr.n
         router[f"m{m}"] = {"us": round(us, 2), "tbps": round(nbytes / us / 1e6, 3),
                            "frac_hbm": round(nbytes / us / 1e3 / pk["hbm_gbs"], 4),
-                           "rel_err_vs_fp64": float(f"{rel:.3g}"), "parity": "ok" if rel <= 1e-5 else "FAIL"}
+                           "rel_err_vs_fp64": float(f"{rel:.3g}"), "parity": "ok" if rel <= 1e-5 else "FAIL",
+                           "path": "tcgen05 (hi/lo in TMEM)" if m > 256 else "hi/lo GEMV (mma.sync)"}
         par_ok &= rel <= 1e-5
     del prs, st_r
     torch.cuda.empty_cache()
