@@ -191,6 +191,7 @@ int mbp_f32_to_bf16(const float* in, uint16_t* out, long long n, cudaStream_t st
 #define MBP_TP_BARRIER 0
 #define MBP_TP_GATHER_BF16 1
 #define MBP_TP_SUM_F32 2
+#define MBP_TP_RSAG 3
 #define MBP_OUT_BF16 0
 #define MBP_OUT_F32 1
 #define MBP_OUT_TAGGED_BF16X2 2
@@ -210,7 +211,11 @@ int mbp_tp_finish(int* const* flags, int rank, int P, int* counter, const void* 
  * MBP_DEV_TIMEOUT_PEER) for the same tiles from the other ranks in its own buffer and writes them into `out`
  * [m][n] (BF16): gathered columns (MBP_TP_GATHER_BF16, column-parallel: w holds rows [rank*n/P, (rank+1)*n/P))
  * or the rank-order sum of the FP32 partials (MBP_TP_SUM_F32, row-parallel: w holds n rows and x's columns
- * [rank*k, (rank+1)*k) for w's k, read in place through ldx).  The grid's last CTA advances the epoch (counter:
+ * [rank*k, (rank+1)*k) for w's k, read in place through ldx: every rank sends its whole partial to every rank),
+ * or the same sum as a reduce-scatter + gather (MBP_TP_RSAG: the tiles of CTA (x, z) belong to rank
+ * (x + z) % P, which alone receives their partials, adds them in rank order and sends the BF16 result as bf16x2
+ * words into every rank's gather region at byte P*32*n*8 of each buffer half, which must hold [32][n/2] words
+ * more: (P-1)/P x 12 m n bytes leave each rank instead of (P-1) x 8 m n).  The grid's last CTA advances the epoch (counter:
  * MBP_TP_COUNTER_SLOTS slots + one ticket int, zero-initialised).  Exchange buffers: two parity halves of
  * m*n/2 (gather) or P*m*n (sum) 64-bit words each.  Every rank makes the same sequence of calls; each rank's
  * grid must fit one wave (the planner's geometries do); graph-replayable. */

@@ -65,6 +65,12 @@ struct __align__(64) GemvParams {
   void* rout;
   int* ctr;
   int rn, rP;
+  // Row-parallel reduce-scatter + gather (MBP_TP_RSAG, tagged f32 words with `rout` set): CTA (x, z)'s tiles are
+  // owned by rank (x + z) % rP; partials go to the owner only, the owner sums them and sends the BF16 result as
+  // bf16x2 words into every rank's gather region (byte offset goff of each buffer half; peer o's region is
+  // outs[o] + gdelta).
+  int rsag, rrank;
+  long long goff, gdelta;
   int nout;
   int C;     // 64-column chunks (k / 64)
   int Rout;  // 16-row tiles computed (n_out / 16)
@@ -152,10 +158,11 @@ MBP_DEV uint32_t bf16x2_bits(float lo, float hi) {
 // The four results (row, tk), (row + 8, tk), (row, tk + 1), (row + 8, tk + 1) of one accumulator as words tagged
 // with `epoch` into every output (the buffer of the epoch's parity).
 template <int OUTK>
-MBP_DEV void emit_tagged(const GemvParams& p, float4 v, int row, int tk, uint32_t epoch) {
+MBP_DEV void emit_tagged(const GemvParams& p, float4 v, int row, int tk, uint32_t epoch, int owner) {
   const uint64_t tag = (uint64_t)epoch << 32;
   const long long par = (long long)(epoch & 1u) * p.parity_stride;
   for (int o = 0; o < p.nout; ++o) {
+    if (p.rsag && o != owner) continue;  // reduce-scatter: the partials go to the tiles' owner only
     uint64_t* out = reinterpret_cast<uint64_t*>(static_cast<char*>(p.outs[o]) + par);
     if constexpr (OUTK == MBP_OUT_TAGGED_BF16X2) {
       const int j = (row >> 4) * 8 + (row & 7);  // word of rows (16*tile + g, 16*tile + g + 8), g = row % 8
@@ -171,6 +178,20 @@ MBP_DEV void emit_tagged(const GemvParams& p, float4 v, int row, int tk, uint32_
         st_relaxed_sys_u64(out + (size_t)(tk + 1) * p.ldo + row + 8, tag | __float_as_uint(v.w));
       }
     }
+  }
+}
+
+// Eight consecutive tagged words: all eight loads are issued before any is checked (one round trip when they
+// have arrived), then each word not yet carrying the epoch is waited for (bounded).
+MBP_DEV void wait_tags8(const uint64_t* w, uint32_t (&d)[8], uint32_t epoch, uint64_t& t0, bool& dead,
+                        uint64_t limit) {
+  uint64_t v[8];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) v[g] = ld_relaxed_sys_u64(w + g);
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    if ((uint32_t)(v[g] >> 32) != epoch) v[g] = wait_tag(w + g, epoch, t0, dead, limit);
+    d[g] = (uint32_t)v[g];
   }
 }
 
@@ -194,8 +215,7 @@ MBP_DEV void tp_receive(const GemvParams& p, uint32_t epoch, int r0, int rvalid,
       const int q = it / per_q, rest = it - q * per_q, rr = rest / ntok, t = tok0 + rest - rr * ntok;
       const uint64_t* w = words + (size_t)t * half + q * (ns / 2) + (r0 + rr) * 8;
       uint32_t d[8];
-#pragma unroll
-      for (int g = 0; g < 8; ++g) d[g] = (uint32_t)wait_tag(w + g, epoch, t0, dead, p.wait_ns);
+      wait_tags8(w, d, epoch, t0, dead, p.wait_ns);
       uint4 lo, hi;
       lo.x = (d[0] & 0xffffu) | d[1] << 16;
       lo.y = (d[2] & 0xffffu) | d[3] << 16;
@@ -216,14 +236,94 @@ MBP_DEV void tp_receive(const GemvParams& p, uint32_t epoch, int r0, int rvalid,
       float a[4];
       for (int q = 0; q < p.rP; ++q) {
         const uint64_t* w = words + ((size_t)q * p.m + t) * p.rn + row;
+        uint64_t v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = ld_relaxed_sys_u64(w + j);  // one round trip for the four
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float f = __uint_as_float((uint32_t)wait_tag(w + j, epoch, t0, dead, p.wait_ns));
+          if ((uint32_t)(v[j] >> 32) != epoch) v[j] = wait_tag(w + j, epoch, t0, dead, p.wait_ns);
+          const float f = __uint_as_float((uint32_t)v[j]);
           a[j] = q == 0 ? f : a[j] + f;
         }
       }
       *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.rout) + (size_t)t * p.rn + row) =
           make_uint2(bf16x2_bits(a[0], a[1]), bf16x2_bits(a[2], a[3]));
+    }
+  }
+}
+
+// Fused receive of the row-parallel reduce-scatter + gather (MBP_TP_RSAG) for one CTA's tiles (rows
+// (r0 .. r0+rvalid-1) x 16, tokens tok0 ..).  On the tiles' owner: item (rr, t, g) = rows 16(r0+rr) + g and + 8 of
+// token t, the P ranks' partials added in rank order (the same sum the all-to-all form makes), rounded to BF16,
+// written to the output and sent as one bf16x2 word to every other rank's gather region.  On the other ranks:
+// item (rr, t) = the owner's 8 words of that tile row -> 16 BF16 of the output.
+template <int TOK>
+MBP_DEV void tp_receive_rsag(const GemvParams& p, uint32_t epoch, int r0, int rvalid, int tok0, int i0, int istride,
+                             int owner) {
+  const long long par = (long long)(epoch & 1u) * p.parity_stride;
+  const uint64_t* words = reinterpret_cast<const uint64_t*>(p.rbuf + par);
+  const int ntok = min(TOK, p.m - tok0);
+  if (ntok <= 0 || rvalid <= 0) return;
+  const int half = p.rn / 2;
+  uint64_t t0 = 0;
+  bool dead = false;
+  if (p.rrank == owner) {
+    const uint64_t tag = (uint64_t)epoch << 32;
+    const int per_r = ntok * 8;
+    for (int it = i0; it < rvalid * per_r; it += istride) {
+      const int rr = it / per_r, rest = it - rr * per_r, t = tok0 + (rest >> 3), g = rest & 7;
+      const int row = (r0 + rr) * 16 + g;
+      // every rank's two words loaded before any is checked: one round trip once they have all arrived
+      const size_t qs = (size_t)p.m * p.rn;
+      const uint64_t* w0 = words + (size_t)t * p.rn + row;
+      uint64_t v[2 * kMaxOuts];
+#pragma unroll
+      for (int q = 0; q < kMaxOuts; ++q)
+        if (q < p.rP) {
+          v[2 * q] = ld_relaxed_sys_u64(w0 + q * qs);
+          v[2 * q + 1] = ld_relaxed_sys_u64(w0 + q * qs + 8);
+        }
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int q = 0; q < kMaxOuts; ++q)
+        if (q < p.rP) {
+          if ((uint32_t)(v[2 * q] >> 32) != epoch) v[2 * q] = wait_tag(w0 + q * qs, epoch, t0, dead, p.wait_ns);
+          if ((uint32_t)(v[2 * q + 1] >> 32) != epoch)
+            v[2 * q + 1] = wait_tag(w0 + q * qs + 8, epoch, t0, dead, p.wait_ns);
+          const float f0 = __uint_as_float((uint32_t)v[2 * q]), f1 = __uint_as_float((uint32_t)v[2 * q + 1]);
+          a0 = q == 0 ? f0 : a0 + f0;
+          a1 = q == 0 ? f1 : a1 + f1;
+        }
+      const uint32_t b2 = bf16x2_bits(a0, a1);
+      uint16_t* o = static_cast<uint16_t*>(p.rout) + (size_t)t * p.rn + row;
+      o[0] = (uint16_t)(b2 & 0xffffu);
+      o[8] = (uint16_t)(b2 >> 16);
+      const size_t wi = (size_t)t * half + (r0 + rr) * 8 + g;
+      for (int q = 0; q < p.rP; ++q) {
+        if (q == p.rrank) continue;
+        uint64_t* gq = reinterpret_cast<uint64_t*>(static_cast<char*>(p.outs[q]) + p.gdelta + par);
+        st_relaxed_sys_u64(gq + wi, tag | b2);
+      }
+    }
+  } else {
+    const uint64_t* gw = reinterpret_cast<const uint64_t*>(p.rbuf + p.goff + par);
+    for (int it = i0; it < rvalid * ntok; it += istride) {
+      const int rr = it / ntok, t = tok0 + it - rr * ntok;
+      const uint64_t* w = gw + (size_t)t * half + (r0 + rr) * 8;
+      uint32_t d[8];
+      wait_tags8(w, d, epoch, t0, dead, p.wait_ns);
+      uint4 lo, hi;
+      lo.x = (d[0] & 0xffffu) | d[1] << 16;
+      lo.y = (d[2] & 0xffffu) | d[3] << 16;
+      lo.z = (d[4] & 0xffffu) | d[5] << 16;
+      lo.w = (d[6] & 0xffffu) | d[7] << 16;
+      hi.x = (d[0] >> 16) | (d[1] & 0xffff0000u);
+      hi.y = (d[2] >> 16) | (d[3] & 0xffff0000u);
+      hi.z = (d[4] >> 16) | (d[5] & 0xffff0000u);
+      hi.w = (d[6] >> 16) | (d[7] & 0xffff0000u);
+      uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.rout) + (size_t)t * p.rn + (r0 + rr) * 16);
+      o[0] = lo;
+      o[1] = hi;
     }
   }
 }
@@ -557,13 +657,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   // dependent, advances the counter only after this grid has completed.
   uint32_t epoch = 0;
   if constexpr (OUTK >= MBP_OUT_TAGGED_BF16X2) epoch = (uint32_t)__ldcg(p.epoch) + 1u;
+  const int owner = p.rsag ? (int)((blockIdx.x + blockIdx.z) % (unsigned)p.rP) : -1;
   auto emit = [&](int idx, float4 v) {
     const int ln = idx & 31, rest = idx >> 5, n = rest % MT, rr = rest / MT;
     if (rr >= rvalid) return;
     const int row = (r0 + rr) * 16 + (ln >> 2);
     const int tk = tok0 + n * 8 + 2 * (ln & 3);
     if constexpr (OUTK >= MBP_OUT_TAGGED_BF16X2) {
-      emit_tagged<OUTK>(p, v, row, tk, epoch);
+      emit_tagged<OUTK>(p, v, row, tk, epoch, owner);
     } else {
       for (int o = 0; o < p.nout; ++o) {
         OutT* out = reinterpret_cast<OutT*>(p.outs[o]);
@@ -624,7 +725,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) k_gemv(const __grid_constant__
   if constexpr (OUTK >= MBP_OUT_TAGGED_BF16X2) {
     if (p.rout) {  // fused receive: this CTA's tiles from every rank, then the epoch ticket
       const int crank = p.split > 1 ? (int)cluster_rank() : 0;
-      tp_receive<OUTK, TOK>(p, epoch, r0, rvalid, tok0, crank * nthr + tid, nthr * p.split);
+      if (OUTK == MBP_OUT_TAGGED_F32 && p.rsag)
+        tp_receive_rsag<TOK>(p, epoch, r0, rvalid, tok0, crank * nthr + tid, nthr * p.split, owner);
+      else
+        tp_receive<OUTK, TOK>(p, epoch, r0, rvalid, tok0, crank * nthr + tid, nthr * p.split);
       tp_advance_epoch(p.ctr, tid);
     }
   }
@@ -923,6 +1027,8 @@ struct RecvArgs {  // fused receive of a tensor-parallel exchange (mbp_gemv_c12_
   void* out;
   int* ctr;
   int n, P;
+  int rsag, rank;  // row-parallel reduce-scatter + gather: this rank, and the gather region's offsets
+  long long goff, gdelta;
 };
 
 int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* esc_off, const uint32_t* esc,
@@ -983,6 +1089,10 @@ int launch(int fmt, const uint8_t* units, const uint8_t* bases, const int32_t* e
   p.ctr = recv ? recv->ctr : nullptr;
   p.rn = recv ? recv->n : 0;
   p.rP = recv ? recv->P : 0;
+  p.rsag = recv ? recv->rsag : 0;
+  p.rrank = recv ? recv->rank : 0;
+  p.goff = recv ? recv->goff : 0;
+  p.gdelta = recv ? recv->gdelta : 0;
   p.nout = nout;
   p.C = C;
   p.Rout = Rout;
@@ -1080,7 +1190,7 @@ int mbp_gemv_c12_tp(const mbp_c12* w, const uint16_t* x, int ldx, int m, const m
   if (!w || !w->units || !w->bases || !w->esc_off || !x || !ex || !out || !ex->counter) return MBP_ERR_ARG;
   if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
   if (ex->P < 1 || ex->P > kMaxOuts || ex->rank < 0 || ex->rank >= ex->P) return MBP_ERR_SHAPE;
-  if (ex->mode != MBP_TP_GATHER_BF16 && ex->mode != MBP_TP_SUM_F32) return MBP_ERR_ARG;
+  if (ex->mode != MBP_TP_GATHER_BF16 && ex->mode != MBP_TP_SUM_F32 && ex->mode != MBP_TP_RSAG) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766) return MBP_ERR_SHAPE;
   const bool gather = ex->mode == MBP_TP_GATHER_BF16;
   if (ex->n != (gather ? w->n * ex->P : w->n)) return MBP_ERR_SHAPE;
@@ -1092,7 +1202,14 @@ int mbp_gemv_c12_tp(const mbp_c12* w, const uint16_t* x, int ldx, int m, const m
     if (!ex->bufs[r]) return MBP_ERR_ARG;
     outs[r] = static_cast<char*>(ex->bufs[r]) + off;
   }
-  RecvArgs rv{static_cast<const uint8_t*>(ex->bufs[ex->rank]), out, ex->counter, ex->n, ex->P};
+  RecvArgs rv{static_cast<const uint8_t*>(ex->bufs[ex->rank]), out, ex->counter, ex->n, ex->P, 0, ex->rank, 0, 0};
+  if (ex->mode == MBP_TP_RSAG) {
+    // gather region after the P slots sized for 32 tokens: [32][n/2] words
+    rv.rsag = 1;
+    rv.goff = (long long)ex->P * 32 * ex->n * 8;
+    rv.gdelta = rv.goff - off;
+    if (ex->parity_stride < rv.goff + 32LL * (ex->n / 2) * 8) return MBP_ERR_SHAPE;
+  }
   return launch(FMT_C12, w->units, w->bases, w->esc_off, w->esc, esc_class(w->n_esc, w->n, w->k), w->k / 64, w->k,
                 w->n, x, ldx, m, outs, ex->P, gather ? ex->n / 2 : ex->n, !gather, geom, stream, ex->counter,
                 ex->parity_stride, gather ? MBP_OUT_TAGGED_BF16X2 : MBP_OUT_TAGGED_F32, &rv);

@@ -25,6 +25,7 @@ DEVICE_STATUS = {1: "consumer timed out waiting for a stage", 2: "producer timed
 
 TP_COUNTER_SLOTS = 64                                    # MBP_TP_COUNTER_SLOTS
 TP_BARRIER, TP_GATHER_BF16, TP_SUM_F32 = 0, 1, 2         # MBP_TP_* modes of mbp_tp_finish
+TP_RSAG = 3                                                # MBP_TP_RSAG: fused row-parallel reduce-scatter + gather
 OUT_BF16, OUT_F32, OUT_TAGGED_BF16X2, OUT_TAGGED_F32 = 0, 1, 2, 3  # MBP_OUT_* kinds of mbp_gemv_c12_multi
 
 

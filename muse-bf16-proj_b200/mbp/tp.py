@@ -38,7 +38,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-from ._lib import (OUT_TAGGED_BF16X2, OUT_TAGGED_F32, TP_BARRIER, TP_COUNTER_SLOTS, TP_GATHER_BF16, TP_SUM_F32,
+from ._lib import (OUT_TAGGED_BF16X2, OUT_TAGGED_F32, TP_BARRIER, TP_COUNTER_SLOTS, TP_GATHER_BF16, TP_RSAG, TP_SUM_F32,
                    TPExchange, check, lib)
 from .ops import BASE_TILE, PackedC12, gemm, gemv, pack_c12
 
@@ -227,11 +227,17 @@ class TPLinear:
     GPUs peer-capable), "nccl" runs the GEMV then an NCCL collective, "auto" picks "p2p" when the group spans
     more than one GPU of this node and NCCL otherwise (the GEMM calls, m > 32, always use NCCL).
     ``fused`` (p2p): one kernel per call (``mbp_gemv_c12_tp``: the GEMV's CTAs also wait for and assemble their
-    tiles from the other ranks); False runs the GEMV and then the separate receive kernel (``mbp_tp_finish``)."""
+    tiles from the other ranks); False runs the GEMV and then the separate receive kernel (``mbp_tp_finish``).
+    ``row_exchange`` (p2p, row-parallel, fused): "sum" sends every rank's FP32 partial to every rank; "rsag" sends
+    each tile's partials to one owner rank, which adds them and sends the BF16 result to all (reduce-scatter +
+    gather: (P-1)/P x 12 m n bytes per rank instead of (P-1) x 8 m n); "auto" = "rsag" from 4 ranks on.  Both
+    give the same bits (rank-order FP32 sums)."""
 
     def __init__(self, w: torch.Tensor, mode: str, group=None, reduce: str = "all", base_mode: int = BASE_TILE,
-                 transport: str = "auto", fused: bool = True):
+                 transport: str = "auto", fused: bool = True, row_exchange: str = "auto"):
         self.fused = fused
+        if row_exchange not in ("auto", "sum", "rsag"):
+            raise ValueError(row_exchange)
         self._two_kernel_m: set = set()
         self.group = group
         world = dist.get_world_size(group)
@@ -243,6 +249,7 @@ class TPLinear:
         if transport not in ("auto", "p2p", "nccl"):
             raise ValueError(transport)
         self.reduce = reduce
+        self.row_exchange = ("rsag" if world >= 4 else "sum") if row_exchange == "auto" else row_exchange
         dev = torch.device("cuda", torch.cuda.current_device())
         self.packed: PackedC12 = pack_c12(self.plan.shard(w.to(dev)), base_mode)
         if transport == "auto":
@@ -259,6 +266,7 @@ class TPLinear:
             per = GEMV_MAX_M * (p.n // 2) * 8                                # [m_max][n/2] bf16-pair words
         else:
             per = p.world * GEMV_MAX_M * p.n * 8                             # [P][m_max][n] f32 words
+            per += GEMV_MAX_M * (p.n // 2) * 8                               # + the reduce-scatter's gather region
         self._sync = _group_sync(self.group)
         self._par = -(-per // 256) * 256                                       # parity-1 buffer offset
         self._xbuf = PeerBuffer(2 * self._par, self.group)
@@ -268,7 +276,8 @@ class TPLinear:
         ex.parity_stride = self._par
         ex.counter = self._sync.counter.data_ptr()
         ex.rank, ex.P, ex.n = p.rank, p.world, p.n
-        ex.mode = TP_GATHER_BF16 if p.mode == "column" else TP_SUM_F32
+        ex.mode = (TP_GATHER_BF16 if p.mode == "column" else
+                   TP_RSAG if self.row_exchange == "rsag" else TP_SUM_F32)
         self._ex = ex
 
     def _forward_p2p(self, x: torch.Tensor) -> torch.Tensor:

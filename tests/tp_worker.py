@@ -2,7 +2,8 @@
 
 Column-parallel fused QKV+gate (K=6144, N=14336, all-gather) and row-parallel output
 projection (K=N=6144, all-reduce and reduce-scatter) at M in {1, 8, 32, 256}, through every transport (NCCL
-collectives; the GEMV's epoch-tagged peer stores with the receive fused into the GEMV, and with the separate
+collectives; the GEMV's epoch-tagged peer stores with the receive fused into the GEMV -- row-parallel as an
+all-to-all of the partials or as a reduce-scatter to each tile's owner plus a gather -- and with the separate
 receive kernel), checked against the FP32 reference of the unsharded projection (rtol 1e-2 / atol 1e-2).  The
 peer-store paths are also checked for: identical bits on every rank, identical column outputs to the NCCL path
 (same per-shard GEMV), identical row outputs of the fused and two-kernel forms, back-to-back calls alternating
@@ -59,6 +60,9 @@ def main():
         layers[tr] = {"column": TPLinear(w_qkv, "column", **kw),
                       "row-all": TPLinear(w_o, "row", reduce="all", **kw)}
     layers["nccl"]["row-scatter"] = TPLinear(w_o, "row", reduce="scatter", transport="nccl")
+    # both fused row-parallel exchanges at every P (the default picks the reduce-scatter + gather from 4 ranks on)
+    layers["p2p-rsag"] = {"row-all": TPLinear(w_o, "row", reduce="all", transport="p2p", row_exchange="rsag")}
+    layers["p2p-sum"] = {"row-all": TPLinear(w_o, "row", reduce="all", transport="p2p", row_exchange="sum")}
     if layers["p2p"]["column"].transport != "p2p":
         fail("p2p transport not selected")
     weights = {"column": w_qkv, "row-all": w_o, "row-scatter": w_o}
@@ -82,8 +86,9 @@ def main():
                     if not torch.equal(out, layers["nccl"]["column"](x)):
                         fail(f"{tr} column m={m}: differs from the NCCL path")
                 if tr == "p2p-two-kernels" and m <= 32 and name == "row-all":
-                    if not torch.equal(out, layers["p2p"]["row-all"](x)):
-                        fail(f"row m={m}: the fused and the two-kernel exchange differ")
+                    for other in ("p2p", "p2p-rsag", "p2p-sum"):
+                        if not torch.equal(out, layers[other]["row-all"](x)):
+                            fail(f"row m={m}: the {other} and the two-kernel exchange differ")
 
     # 2. back-to-back calls on one stream (the exchange buffers alternate); outputs read before the next call
     col, row = layers["p2p"]["column"], layers["p2p"]["row-all"]
@@ -138,7 +143,7 @@ def main():
     # a released layer refuses further calls
     xbytes = sum(lin._xbuf.nbytes for ls in layers.values() for lin in ls.values() if lin._xbuf is not None)
     free0 = torch.cuda.mem_get_info()[0]
-    for tr in ("nccl", "p2p", "p2p-two-kernels"):
+    for tr in ("nccl", "p2p", "p2p-two-kernels", "p2p-rsag", "p2p-sum"):
         release_tp({"tp": layers[tr]})
     torch.cuda.synchronize()
     freed = torch.cuda.mem_get_info()[0] - free0
