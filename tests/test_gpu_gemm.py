@@ -78,6 +78,21 @@ def test_gemm_odd_chunk_counts(n, k, m):
     assert mbp.device_status() == 0
 
 
+@pytest.mark.parametrize("n,k,m", [(14288, 1024, 128), (14336, 576, 64), (12048, 640, 100)])
+def test_gemm_uneven_row_blocks(n, k, m):
+    """Shapes whose 128-row blocks would leave SMs idle without a K split: the row tiles are spread over one wave
+    of blocks holding 6-8 tiles each (the box's other rows are neither decoded nor stored)."""
+    import mbp
+    w = weight(n, k, seed=n, escape_frac=0.01)
+    p = mbp.pack_c12(w)
+    x = tokens(m, k, seed=m)
+    out = mbp.gemm(p, x, out_dtype=torch.float32)
+    ref = torch.cat([mbp.gemv(p, x[i:i + 32].contiguous(), out_dtype=torch.float32) for i in range(0, m, 32)])
+    assert torch.allclose(out, ref, rtol=1e-4, atol=1e-3)
+    assert_close_bf16(mbp.gemm(p, x), ref_f32(x, w))
+    assert mbp.device_status() == 0
+
+
 def test_gemm_partial_rows_and_f32():
     import mbp
     w = weight(8192, 1024, seed=5, escape_frac=0.01)
