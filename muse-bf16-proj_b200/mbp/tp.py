@@ -216,6 +216,16 @@ class TPPlan:
         return self.rank * s, (self.rank + 1) * s
 
 
+def row_exchange_for(world: int, requested: str = "auto") -> str:
+    """The fused row-parallel exchange a layer of `world` ranks uses: "sum" (every rank's FP32 partial to every
+    rank) or "rsag" (reduce-scatter to each tile's owner + BF16 gather); "auto" = "rsag" from 4 ranks on."""
+    if requested not in ("auto", "sum", "rsag"):
+        raise ValueError(f"row_exchange must be auto, sum or rsag, got {requested!r}")
+    if requested != "auto":
+        return requested
+    return "rsag" if world >= 4 else "sum"
+
+
 def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
@@ -236,8 +246,6 @@ class TPLinear:
     def __init__(self, w: torch.Tensor, mode: str, group=None, reduce: str = "all", base_mode: int = BASE_TILE,
                  transport: str = "auto", fused: bool = True, row_exchange: str = "auto"):
         self.fused = fused
-        if row_exchange not in ("auto", "sum", "rsag"):
-            raise ValueError(row_exchange)
         self._two_kernel_m: set = set()
         self.group = group
         world = dist.get_world_size(group)
@@ -249,7 +257,7 @@ class TPLinear:
         if transport not in ("auto", "p2p", "nccl"):
             raise ValueError(transport)
         self.reduce = reduce
-        self.row_exchange = ("rsag" if world >= 4 else "sum") if row_exchange == "auto" else row_exchange
+        self.row_exchange = row_exchange_for(world, row_exchange)
         dev = torch.device("cuda", torch.cuda.current_device())
         self.packed: PackedC12 = pack_c12(self.plan.shard(w.to(dev)), base_mode)
         if transport == "auto":

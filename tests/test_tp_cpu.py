@@ -162,3 +162,11 @@ def test_peer_store_placement_rule():
     assert not _p2p_placement_ok(seen(["GPU-0", "GPU-1"]), "h", local, 0, lambda a, b: False)  # no peer access
     # a peer this process cannot see (per-rank device lists): its buffer's IPC mapping is unknown, so NCCL
     assert not _p2p_placement_ok(seen(["GPU-0", "GPU-5"]), "h", {"GPU-0": 0}, 0, peers)
+
+
+def test_row_exchange_choice():
+    from mbp.tp import row_exchange_for
+    assert row_exchange_for(2) == "sum" and row_exchange_for(4) == "rsag" and row_exchange_for(8) == "rsag"
+    assert row_exchange_for(8, "sum") == "sum" and row_exchange_for(2, "rsag") == "rsag"
+    with pytest.raises(ValueError):
+        row_exchange_for(4, "ring")
