@@ -389,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       uint32_t A[16];
       uint32_t dep = 0;
       if (!live) {
+        // nothing to load: the arrive below hands the stage back at once
       } else if constexpr (HILO) {
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
@@ -396,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
           A[4 * qq] = v.x, A[4 * qq + 1] = v.y, A[4 * qq + 2] = v.z, A[4 * qq + 3] = v.w;
         }
         dep = A[0] ^ A[4] ^ A[8] ^ A[12];  // a value from each load
-      } else if (live) {
+      } else {
         const uint4 p0 = *reinterpret_cast<const uint4*>(u);
         const uint4 p1 = *reinterpret_cast<const uint4*>(u + 512);
         const uint4 p2 = *reinterpret_cast<const uint4*>(u + 1024);
