@@ -775,8 +775,9 @@ def run_mbp_tp(args, rank, world):
                                         "parity": "ok" if ok1 else "FAIL",
                                         "path": ("GEMV + " + ("peer-store exchange" if transport == "p2p"
                                                               else "NCCL")) if m <= mbp.GEMV_MAX_M
-                                        else "tcgen05 GEMM + NCCL " + ("all-gather" if layer == "qkv_gate"
-                                                                       else "all-reduce")}
+                                        else ("tcgen05 GEMM + peer-store exchange" if layer == "qkv_gate"
+                                              and transport == "p2p" else "tcgen05 GEMM + NCCL "
+                                              + ("all-gather" if layer == "qkv_gate" else "all-reduce"))}
     del flush
     torch.cuda.synchronize()
     status_ok &= mbp.device_status() == 0

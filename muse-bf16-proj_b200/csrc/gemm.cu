@@ -79,6 +79,14 @@ struct __align__(64) GemmParams {
   int f32out;
   int wsubs;                   // sub-tiles per weight box: 2 (1 for a 12-bit matrix of a single chunk)
   int nblk;                    // row blocks: block b owns row tiles [b*Rout/nblk, (b+1)*Rout/nblk), at most 8
+  // Tensor-parallel column gather (nout > 0): instead of `out`, every result pair (rows 16*tile + g and + 8) goes
+  // as one epoch-tagged bf16x2 word (tok, 8*tile + g) into each of the nout exchange buffers (ldo in words; the
+  // buffer half of the epoch's parity), epoch = *epoch + 1; the layout mbp_gemv_c12_multi's MBP_OUT_TAGGED_BF16X2
+  // writes and mbp_tp_finish's MBP_TP_GATHER_BF16 reads.
+  void* touts[8];
+  int nout;
+  const int* epoch;
+  long long parity_stride;
   unsigned long long wait_ns;  // limit of every bounded wait
 };
 
@@ -201,6 +209,19 @@ MBP_DEV void tc_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+MBP_DEV uint32_t bf16_pair(float lo, float hi) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(lo)) | (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16;
+}
+
+// One tagged exchange word (rows row and row + 8 of a 16-row tile, row % 16 < 8) into every exchange buffer.
+MBP_DEV void store_tagged(const GemmParams& p, int tok, int row, float lo, float hi, uint32_t epoch) {
+  const uint64_t w = (uint64_t)epoch << 32 | bf16_pair(lo, hi);
+  const long long par = (long long)(epoch & 1u) * p.parity_stride;
+  const size_t idx = (size_t)tok * p.ldo + (size_t)(row >> 4) * 8 + (row & 7);
+  for (int o = 0; o < p.nout; ++o)
+    st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(static_cast<char*>(p.touts[o]) + par) + idx, w);
 }
 
 MBP_DEV void store_elem(const GemmParams& p, int tok, int row, float f) {
@@ -431,6 +452,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
   const int ncol = (p.bn + 31) / 32;
   const int row_l = q * 32 + lane;                 // row inside the 128-row tile
   const int row = rb0 * 16 + row_l;                // global output row
+  // the exchange epoch (after this grid's dependency wait: the receive kernel after the previous exchange, which
+  // advances the counter, has completed)
+  const uint32_t epoch = p.nout > 0 ? (uint32_t)__ldcg(p.epoch) + 1u : 0u;
   bool ok = true;
   if (epi) {
     ok = mbar_wait(done, 0, MBP_DEV_TIMEOUT_MMA, p.wait_ns);
@@ -442,7 +466,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       for (int cc = part; cc < ncol; cc += nparts) {
         uint32_t v[32];
         tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32), v);
-        if (row_l < rvalid * 16) {
+        if (p.nout > 0) {
+          // tagged pairs: row g + 8 of a tile is lane + 8 of the same warp (the shuffle runs on the whole warp)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float f = __uint_as_float(v[j]);
+            const float fh = __shfl_down_sync(0xffffffffu, f, 8);
+            const int tok = tok0 + cc * 32 + j;
+            if ((lane & 8) == 0 && row_l < rvalid * 16 && cc * 32 + j < p.bn && tok < p.m)
+              store_tagged(p, tok, row, f, fh, epoch);
+          }
+        } else if (row_l < rvalid * 16) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             // columns past the tile's bn tokens (bn % 32 != 0) belong to the next token tile's CTA
@@ -480,7 +514,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         s += f;
       }
       const int tok = tok0 + c, grow = rb0 * 16 + r;
-      if (c < p.bn && tok < p.m && r < rvalid * 16) store_elem(p, tok, grow, s);
+      if (p.nout > 0) {
+        // a warp holds 32 consecutive rows of one column (640 threads, 128 rows per column): row + 8 is lane + 8
+        const float sh = __shfl_down_sync(0xffffffffu, s, 8);
+        if ((r & 8) == 0 && c < p.bn && tok < p.m && r < rvalid * 16) store_tagged(p, tok, grow, s, sh, epoch);
+      } else if (c < p.bn && tok < p.m && r < rvalid * 16) {
+        store_elem(p, tok, grow, s);
+      }
     }
     cluster_sync();  // keep this CTA's partials alive until every rank has read them
   }
@@ -596,9 +636,16 @@ int sm_count_here() {
 // One launch of k_gemm<hilo>: units/bases/escapes describe the weights (bases and escapes unused for hi/lo),
 // R16 = row tiles of the weights, rout16 = row tiles written, C = 64-column chunks.  bn: token tile; split: K
 // split (cluster size; 0 = choose).
+struct GemmTag {  // tagged exchange outputs (tensor-parallel column gather)
+  void* const* outs;
+  int nout;
+  const int* epoch;
+  long long parity_stride;
+};
+
 int launch_gemm(bool hilo, const uint8_t* units, const uint8_t* bases, const int32_t* esc_off, const uint32_t* esc,
                 int R16, int rout16, int C, const uint16_t* x, int m, void* out, int ldo, bool f32, int bn, int split,
-                int min_split, int max_split, cudaStream_t stream) {
+                int min_split, int max_split, cudaStream_t stream, const GemmTag* tag = nullptr) {
   const GLayout L = gemm_layout(bn, hilo);
   const int smem = L.total + 1024;
   if (smem > kMaxSmem) return MBP_ERR_SMEM;
@@ -625,6 +672,10 @@ int launch_gemm(bool hilo, const uint8_t* units, const uint8_t* bases, const int
   p.bn = bn;
   p.f32out = f32 ? 1 : 0;
   p.wsubs = (hilo || C >= 2) ? 2 : 1;
+  p.nout = tag ? tag->nout : 0;
+  for (int o = 0; o < 8; ++o) p.touts[o] = tag && o < tag->nout ? tag->outs[o] : nullptr;
+  p.epoch = tag ? tag->epoch : nullptr;
+  p.parity_stride = tag ? tag->parity_stride : 0;
   p.wait_ns = wait_limit_ns();
   const int ntok = (m + bn - 1) / bn;
   p.nblk = (p.Rout + 7) / 8;
@@ -665,12 +716,12 @@ int launch_gemm(bool hilo, const uint8_t* units, const uint8_t* bases, const int
 }
 
 int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out, int ldo, bool f32,
-                cudaStream_t stream) {
-  if (!w || !w->units || !w->bases || !w->esc_off || !x || !out) return MBP_ERR_ARG;
+                cudaStream_t stream, const GemmTag* tag = nullptr) {
+  if (!w || !w->units || !w->bases || !w->esc_off || !x || (!out && !tag)) return MBP_ERR_ARG;
   if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n || n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
   if (m < 1) return MBP_ERR_M;
-  if (ldo < n_out) return MBP_ERR_SHAPE;
+  if (tag ? ldo < n_out / 2 : ldo < n_out) return MBP_ERR_SHAPE;  // tagged: ldo in 64-bit words
   if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u)) return MBP_ERR_ALIGN;
   // Token tile: all tokens up to 256.  Short K (<= 2048): a cluster split-K's reduction costs more than its
   // short main loop saves, so smaller token tiles fill the SMs instead, down to 64 while one wave holds them
@@ -688,7 +739,7 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
     }
   }
   return launch_gemm(false, w->units, w->bases, w->esc_off, w->esc, w->n / 16, n_out / 16, w->k / 64, x, m, out,
-                     ldo, f32, bn, 0, 1, 8, stream);
+                     ldo, f32, bn, 0, 1, 8, stream, tag);
 }
 
 }  // namespace
@@ -703,6 +754,20 @@ int mbp_gemm_c12(const mbp_c12* w, const uint16_t* x, int m, int n_out, uint16_t
 int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, float* out, int ldo,
                      cudaStream_t stream) {
   return gemm_launch(w, x, m, n_out, out, ldo, true, stream);
+}
+
+int mbp_gemm_c12_multi(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* const* outs, int nout, int ldo,
+                       int out_kind, const int* epoch, long long parity_stride, cudaStream_t stream) {
+  if (out_kind != MBP_OUT_TAGGED_BF16X2) return MBP_ERR_ARG;
+  if (!outs || nout < 1 || nout > 8 || !epoch) return MBP_ERR_ARG;
+  if (parity_stride < 0 || (parity_stride & 15)) return MBP_ERR_ALIGN;
+  for (int o = 0; o < nout; ++o) {
+    if (!outs[o]) return MBP_ERR_ARG;
+    if ((uintptr_t)outs[o] & 7u) return MBP_ERR_ALIGN;
+  }
+  if (ldo < n_out / 2) return MBP_ERR_SHAPE;
+  const GemmTag tag{outs, nout, epoch, parity_stride};
+  return gemm_launch(w, x, m, n_out, nullptr, ldo, false, stream, &tag);
 }
 
 int mbp_router_hilo_tc(const mbp_hilo* w, const uint16_t* x, int m, float* out, int ldo, int bn, int split,

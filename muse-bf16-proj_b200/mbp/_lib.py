@@ -92,6 +92,7 @@ SIGNATURES = [
     ("mbp_gemm_c12", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
     ("mbp_gemm_c12_f32", _I, [ctypes.POINTER(C12), _P, _I, _I, _P, _I, _P]),
     ("mbp_router_hilo_tc", _I, [ctypes.POINTER(HiLo), _P, _I, _P, _I, _I, _I, _P]),
+    ("mbp_gemm_c12_multi", _I, [ctypes.POINTER(C12), _P, _I, _I, ctypes.POINTER(_P), _I, _I, _I, _P, _I64, _P]),
 ]
 
 _lib = None

@@ -43,6 +43,7 @@ from ._lib import (OUT_TAGGED_BF16X2, OUT_TAGGED_F32, TP_BARRIER, TP_COUNTER_SLO
 from .ops import BASE_TILE, PackedC12, gemm, gemv, pack_c12
 
 GEMV_MAX_M = 32
+GEMM_EXCHANGE_MAX_M = 256  # column-parallel GEMM calls up to this size exchange by peer stores (buffers sized for it)
 _ERR_SPLIT = -3  # MBP_ERR_SPLIT
 
 
@@ -235,7 +236,8 @@ class TPLinear:
 
     ``transport``: "p2p" stores GEMV results straight into the peers' exchange buffers (one node, every pair of
     GPUs peer-capable), "nccl" runs the GEMV then an NCCL collective, "auto" picks "p2p" when the group spans
-    more than one GPU of this node and NCCL otherwise (the GEMM calls, m > 32, always use NCCL).
+    more than one GPU of this node and NCCL otherwise (p2p also carries the column-parallel GEMM calls up to
+    256 tokens; the row-parallel GEMM calls, m > 32, use NCCL).
     ``fused`` (p2p): one kernel per call (``mbp_gemv_c12_tp``: the GEMV's CTAs also wait for and assemble their
     tiles from the other ranks); False runs the GEMV and then the separate receive kernel (``mbp_tp_finish``).
     ``row_exchange`` (p2p, row-parallel, fused): "sum" sends every rank's FP32 partial to every rank; "rsag" sends
@@ -271,7 +273,7 @@ class TPLinear:
         p = self.plan
         # exchange buffers of epoch-tagged 64-bit words, two per rank (epoch parity)
         if p.mode == "column":
-            per = GEMV_MAX_M * (p.n // 2) * 8                                # [m_max][n/2] bf16-pair words
+            per = GEMM_EXCHANGE_MAX_M * (p.n // 2) * 8                       # [m_max][n/2] bf16-pair words
         else:
             per = p.world * GEMV_MAX_M * p.n * 8                             # [P][m_max][n] f32 words
             per += GEMV_MAX_M * (p.n // 2) * 8                               # + the reduce-scatter's gather region
@@ -323,6 +325,22 @@ class TPLinear:
         sync.finish(buf, self._par, TP_SUM_F32, m, p.n, out)
         return out
 
+    def _forward_gemm_p2p(self, x: torch.Tensor) -> torch.Tensor:
+        """Column-parallel call above 32 tokens: the shard's tcgen05 GEMM stores its result as tagged bf16x2 words
+        into every rank's exchange buffer (its columns of the [m][n/2] word grid), then the receive kernel
+        assembles [m, n] from this rank's buffer (the same words, epochs and parity halves as the GEMV calls)."""
+        p = self.plan
+        m = x.shape[0]
+        out = torch.empty((m, p.n), dtype=torch.bfloat16, device=x.device)
+        ns = p.n // p.world
+        sync = self._sync
+        check(lib().mbp_gemm_c12_multi(ctypes.byref(self.packed.desc), ctypes.c_void_p(x.data_ptr()), m, ns,
+                                       self._xbuf.local_first(p.rank * (ns // 2) * 8), p.world, p.n // 2,
+                                       OUT_TAGGED_BF16X2, ctypes.c_void_p(sync.counter.data_ptr()), self._par,
+                                       _stream()), "mbp_gemm_c12_multi")
+        sync.finish(self._xbuf, self._par, TP_GATHER_BF16, m, p.n, out)
+        return out
+
     def _local(self, x: torch.Tensor, out_dtype) -> torch.Tensor:
         xs = self.plan.x_slice(x)
         if xs.shape[0] <= GEMV_MAX_M:
@@ -341,6 +359,12 @@ class TPLinear:
             raise RuntimeError("TPLinear used after close()")
         p = self.plan
         m = x.shape[0]
+        if (self._xbuf is not None and p.mode == "column" and GEMV_MAX_M < m <= GEMM_EXCHANGE_MAX_M):
+            if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != p.k or not x.is_contiguous():
+                raise ValueError(f"x must be a contiguous bf16 [m, {p.k}] tensor")
+            if x.device != self.packed.units.device:
+                raise ValueError("x is not on this rank's device")
+            return self._forward_gemm_p2p(x)
         if self._xbuf is not None and 1 <= m <= GEMV_MAX_M and (p.mode == "column" or self.reduce == "all"):
             if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != p.k or not x.is_contiguous():
                 raise ValueError(f"x must be a contiguous bf16 [m, {p.k}] tensor")

@@ -68,7 +68,7 @@ def main():
     weights = {"column": w_qkv, "row-all": w_o, "row-scatter": w_o}
 
     # 1. every layer, every m, against the FP32 reference
-    for m in (1, 8, 32, 256):
+    for m in (1, 8, 32, 100, 256):
         x = torch.randn(m, 6144, generator=torch.Generator().manual_seed(m)).to(torch.bfloat16).cuda()
         for tr, ls in layers.items():
             for name, lin in ls.items():
