@@ -660,8 +660,9 @@ def run_mbp_tp(args, rank, world):
     + all-gather, O row-parallel + all-reduce of FP32 partials; by default through the GEMV's peer stores with
     the receive fused into it, `--transport nccl` for NCCL collectives).  Total work is fixed (strong scaling);
     value = bytes of the unsharded calls per step / step time (max over ranks).  After timing, every output of
-    the step and of the config-5 calls (M in {1, 32, 256}, through the GEMM + NCCL at M = 256) is compared with
-    the FP32 reference of the full weights and with the unsharded single-GPU kernels."""
+    the step and of the config-5 calls (M in {1, 32, 256}; at M = 256 through the GEMM, exchanging by peer stores
+    for the column gather and, at 2 ranks, the row sum, by NCCL otherwise) is compared with the FP32 reference of
+    the full weights and with the unsharded single-GPU kernels."""
     import torch
     import torch.distributed as dist
     import mbp
@@ -775,8 +776,8 @@ def run_mbp_tp(args, rank, world):
                                         "parity": "ok" if ok1 else "FAIL",
                                         "path": ("GEMV + " + ("peer-store exchange" if transport == "p2p"
                                                               else "NCCL")) if m <= mbp.GEMV_MAX_M
-                                        else ("tcgen05 GEMM + peer-store exchange" if layer == "qkv_gate"
-                                              and transport == "p2p" else "tcgen05 GEMM + NCCL "
+                                        else ("tcgen05 GEMM + peer-store exchange" if transport == "p2p"
+                                              and (layer == "qkv_gate" or world == 2) else "tcgen05 GEMM + NCCL "
                                               + ("all-gather" if layer == "qkv_gate" else "all-reduce"))}
     del flush
     torch.cuda.synchronize()

@@ -200,10 +200,10 @@ int mbp_ipc_alloc(size_t bytes, void** ptr, void* handle64);
 int mbp_ipc_open(const void* handle64, void** ptr);
 int mbp_ipc_close(void* ptr);
 int mbp_ipc_free(void* ptr);
-/* mbp_gemm_c12_multi: the tcgen05 GEMM (any m) storing its result as MBP_OUT_TAGGED_BF16X2 words (the only kind
- * it takes) into `nout` (<= 8) exchange buffers, same layout, epoch and parity rules as mbp_gemv_c12_multi; the
- * receive is mbp_tp_finish with MBP_TP_GATHER_BF16.  The column-parallel exchange of the verify-size calls, in
- * place of an NCCL all-gather and its assembly kernel. */
+/* mbp_gemm_c12_multi: the tcgen05 GEMM (any m) storing its result as MBP_OUT_TAGGED_BF16X2 words (column-parallel
+ * gather; receive: mbp_tp_finish MBP_TP_GATHER_BF16) or MBP_OUT_TAGGED_F32 words (row-parallel partials; receive:
+ * MBP_TP_SUM_F32) into `nout` (<= 8) exchange buffers, same layout, epoch and parity rules as mbp_gemv_c12_multi.
+ * The exchange of the verify-size calls, in place of an NCCL collective and its assembly / rounding kernel. */
 int mbp_gemm_c12_multi(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* const* outs, int nout, int ldo,
                        int out_kind, const int* epoch, long long parity_stride, cudaStream_t stream);
 int mbp_gemv_c12_multi(const mbp_c12* w, const uint16_t* x, int ldx, int m, int n_out, void* const* outs, int nout,

@@ -83,8 +83,10 @@ struct __align__(64) GemmParams {
   // as one epoch-tagged bf16x2 word (tok, 8*tile + g) into each of the nout exchange buffers (ldo in words; the
   // buffer half of the epoch's parity), epoch = *epoch + 1; the layout mbp_gemv_c12_multi's MBP_OUT_TAGGED_BF16X2
   // writes and mbp_tp_finish's MBP_TP_GATHER_BF16 reads.
+  // With tag_f32 set (row-parallel sum), every result goes as its own tagged f32 word (tok, row) instead.
   void* touts[8];
   int nout;
+  int tag_f32;
   const int* epoch;
   long long parity_stride;
   unsigned long long wait_ns;  // limit of every bounded wait
@@ -220,6 +222,15 @@ MBP_DEV void store_tagged(const GemmParams& p, int tok, int row, float lo, float
   const uint64_t w = (uint64_t)epoch << 32 | bf16_pair(lo, hi);
   const long long par = (long long)(epoch & 1u) * p.parity_stride;
   const size_t idx = (size_t)tok * p.ldo + (size_t)(row >> 4) * 8 + (row & 7);
+  for (int o = 0; o < p.nout; ++o)
+    st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(static_cast<char*>(p.touts[o]) + par) + idx, w);
+}
+
+// One tagged f32 word (the row-parallel partial sums) into every exchange buffer.
+MBP_DEV void store_tagged_f32(const GemmParams& p, int tok, int row, float f, uint32_t epoch) {
+  const uint64_t w = (uint64_t)epoch << 32 | __float_as_uint(f);
+  const long long par = (long long)(epoch & 1u) * p.parity_stride;
+  const size_t idx = (size_t)tok * p.ldo + row;
   for (int o = 0; o < p.nout; ++o)
     st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(static_cast<char*>(p.touts[o]) + par) + idx, w);
 }
@@ -466,7 +477,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
       for (int cc = part; cc < ncol; cc += nparts) {
         uint32_t v[32];
         tc_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cc * 32), v);
-        if (p.nout > 0) {
+        if (p.nout > 0 && p.tag_f32) {
+          if (row_l < rvalid * 16) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int tok = tok0 + cc * 32 + j;
+              if (cc * 32 + j < p.bn && tok < p.m) store_tagged_f32(p, tok, row, __uint_as_float(v[j]), epoch);
+            }
+          }
+        } else if (p.nout > 0) {
           // tagged pairs: row g + 8 of a tile is lane + 8 of the same warp (the shuffle runs on the whole warp)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -514,7 +533,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemm(const __grid_constant__ Ge
         s += f;
       }
       const int tok = tok0 + c, grow = rb0 * 16 + r;
-      if (p.nout > 0) {
+      if (p.nout > 0 && p.tag_f32) {
+        if (c < p.bn && tok < p.m && r < rvalid * 16) store_tagged_f32(p, tok, grow, s, epoch);
+      } else if (p.nout > 0) {
         // a warp holds 32 consecutive rows of one column (640 threads, 128 rows per column): row + 8 is lane + 8
         const float sh = __shfl_down_sync(0xffffffffu, s, 8);
         if ((r & 8) == 0 && c < p.bn && tok < p.m && r < rvalid * 16) store_tagged(p, tok, grow, s, sh, epoch);
@@ -636,9 +657,10 @@ int sm_count_here() {
 // One launch of k_gemm<hilo>: units/bases/escapes describe the weights (bases and escapes unused for hi/lo),
 // R16 = row tiles of the weights, rout16 = row tiles written, C = 64-column chunks.  bn: token tile; split: K
 // split (cluster size; 0 = choose).
-struct GemmTag {  // tagged exchange outputs (tensor-parallel column gather)
+struct GemmTag {  // tagged exchange outputs (tensor-parallel column gather, or row-parallel f32 partials)
   void* const* outs;
   int nout;
+  int f32;
   const int* epoch;
   long long parity_stride;
 };
@@ -673,6 +695,7 @@ int launch_gemm(bool hilo, const uint8_t* units, const uint8_t* bases, const int
   p.f32out = f32 ? 1 : 0;
   p.wsubs = (hilo || C >= 2) ? 2 : 1;
   p.nout = tag ? tag->nout : 0;
+  p.tag_f32 = tag ? tag->f32 : 0;
   for (int o = 0; o < 8; ++o) p.touts[o] = tag && o < tag->nout ? tag->outs[o] : nullptr;
   p.epoch = tag ? tag->epoch : nullptr;
   p.parity_stride = tag ? tag->parity_stride : 0;
@@ -721,7 +744,7 @@ int gemm_launch(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* out
   if (w->n_esc > 0 && !w->esc) return MBP_ERR_ARG;
   if (w->n % 16 || w->k % 64 || w->k / 64 > 32766 || n_out > w->n || n_out <= 0 || n_out % 16) return MBP_ERR_SHAPE;
   if (m < 1) return MBP_ERR_M;
-  if (tag ? ldo < n_out / 2 : ldo < n_out) return MBP_ERR_SHAPE;  // tagged: ldo in 64-bit words
+  if (tag ? ldo < (tag->f32 ? n_out : n_out / 2) : ldo < n_out) return MBP_ERR_SHAPE;  // tagged: ldo in words
   if (((uintptr_t)x & 15u) || ((uintptr_t)w->units & 15u)) return MBP_ERR_ALIGN;
   // Token tile: all tokens up to 256.  Short K (<= 2048): a cluster split-K's reduction costs more than its
   // short main loop saves, so smaller token tiles fill the SMs instead, down to 64 while one wave holds them
@@ -758,15 +781,16 @@ int mbp_gemm_c12_f32(const mbp_c12* w, const uint16_t* x, int m, int n_out, floa
 
 int mbp_gemm_c12_multi(const mbp_c12* w, const uint16_t* x, int m, int n_out, void* const* outs, int nout, int ldo,
                        int out_kind, const int* epoch, long long parity_stride, cudaStream_t stream) {
-  if (out_kind != MBP_OUT_TAGGED_BF16X2) return MBP_ERR_ARG;
+  if (out_kind != MBP_OUT_TAGGED_BF16X2 && out_kind != MBP_OUT_TAGGED_F32) return MBP_ERR_ARG;
+  const bool f32 = out_kind == MBP_OUT_TAGGED_F32;
   if (!outs || nout < 1 || nout > 8 || !epoch) return MBP_ERR_ARG;
   if (parity_stride < 0 || (parity_stride & 15)) return MBP_ERR_ALIGN;
   for (int o = 0; o < nout; ++o) {
     if (!outs[o]) return MBP_ERR_ARG;
     if ((uintptr_t)outs[o] & 7u) return MBP_ERR_ALIGN;
   }
-  if (ldo < n_out / 2) return MBP_ERR_SHAPE;
-  const GemmTag tag{outs, nout, epoch, parity_stride};
+  if (ldo < (f32 ? n_out : n_out / 2)) return MBP_ERR_SHAPE;
+  const GemmTag tag{outs, nout, f32 ? 1 : 0, epoch, parity_stride};
   return gemm_launch(w, x, m, n_out, nullptr, ldo, false, stream, &tag);
 }
 

@@ -52,7 +52,7 @@ __global__ void k_f32_to_bf16(const float4* __restrict__ src, uint2* __restrict_
 
 constexpr int kMaxRanks = 8;
 constexpr int kSlots = MBP_TP_COUNTER_SLOTS;  // a receive launch has one block per epoch slot
-constexpr int kRecvThreads = 256;
+constexpr int kRecvThreads = 1024;  // the receive of a 256-token exchange has ~400 K items for 64 blocks
 
 struct TPFinish {
   int* flags[kMaxRanks];  // flags[r] = rank r's flag array (kMaxRanks ints), as mapped in this process
@@ -123,9 +123,15 @@ __global__ void __launch_bounds__(kRecvThreads) k_tp_recv(const __grid_constant_
     for (long long i = i0; i < items; i += stride) {
       const int t = (int)(i / tiles), tile = (int)(i - (long long)t * tiles);
       const uint64_t* w = words + (long long)t * (s.n / 2) + tile * 8;
+      uint64_t v[8];
+#pragma unroll
+      for (int g = 0; g < 8; ++g) v[g] = ld_relaxed_sys_u64(w + g);  // all eight before any check: one round trip
       uint32_t d[8];
 #pragma unroll
-      for (int g = 0; g < 8; ++g) d[g] = (uint32_t)wait_tag(w + g, e, t0, dead, s.wait_ns);
+      for (int g = 0; g < 8; ++g) {
+        if ((uint32_t)(v[g] >> 32) != e) v[g] = wait_tag(w + g, e, t0, dead, s.wait_ns);
+        d[g] = (uint32_t)v[g];
+      }
       uint4 lo, hi;
       lo.x = (d[0] & 0xffffu) | d[1] << 16;
       lo.y = (d[2] & 0xffffu) | d[3] << 16;
@@ -146,13 +152,28 @@ __global__ void __launch_bounds__(kRecvThreads) k_tp_recv(const __grid_constant_
     for (long long i = i0; i < items; i += stride) {
       const int t = (int)(i / q4), c = (int)(i - (long long)t * q4) * 4;
       float a[4];
-      for (int r = 0; r < s.P; ++r) {
-        const uint64_t* w = words + ((long long)r * s.m + t) * s.n + c;
+      const long long rs = (long long)s.m * s.n;
+      const uint64_t* w0 = words + (long long)t * s.n + c;
+      for (int r0 = 0; r0 < s.P; r0 += 2) {  // two ranks' four words before any check: one round trip per pair
+        const int nr = s.P - r0 < 2 ? s.P - r0 : 2;
+        uint64_t v[2][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float f = __uint_as_float((uint32_t)wait_tag(w + j, e, t0, dead, s.wait_ns));
-          a[j] = r == 0 ? f : a[j] + f;
-        }
+        for (int h = 0; h < 2; ++h)
+          if (h < nr) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[h][j] = ld_relaxed_sys_u64(w0 + (r0 + h) * rs + j);
+          }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          if (h < nr) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint64_t* wj = w0 + (r0 + h) * rs + j;
+              if ((uint32_t)(v[h][j] >> 32) != e) v[h][j] = wait_tag(wj, e, t0, dead, s.wait_ns);
+              const float f = __uint_as_float((uint32_t)v[h][j]);
+              a[j] = r0 + h == 0 ? f : a[j] + f;
+            }
+          }
       }
       reinterpret_cast<uint2*>(s.out)[i] = make_uint2(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]));
     }

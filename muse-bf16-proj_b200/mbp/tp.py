@@ -277,6 +277,8 @@ class TPLinear:
         else:
             per = p.world * GEMV_MAX_M * p.n * 8                             # [P][m_max][n] f32 words
             per += GEMV_MAX_M * (p.n // 2) * 8                               # + the reduce-scatter's gather region
+            if self._gemm_row_p2p():
+                per = max(per, p.world * GEMM_EXCHANGE_MAX_M * p.n * 8)      # the GEMM calls' [P][m][n] partials
         self._sync = _group_sync(self.group)
         self._par = -(-per // 256) * 256                                       # parity-1 buffer offset
         self._xbuf = PeerBuffer(2 * self._par, self.group)
@@ -325,20 +327,35 @@ class TPLinear:
         sync.finish(buf, self._par, TP_SUM_F32, m, p.n, out)
         return out
 
+    def _gemm_row_p2p(self) -> bool:
+        """Row-parallel GEMM calls exchange their FP32 partials by peer stores at 2 ranks only: every rank sends
+        its whole [m][n] partial to every rank, (P-1) x 8 m n bytes, which beats NCCL's all-reduce at P = 2 but not
+        beyond (at 256 tokens and P = 8, 88 MB per rank)."""
+        return self.plan.mode == "row" and self.plan.world == 2
+
     def _forward_gemm_p2p(self, x: torch.Tensor) -> torch.Tensor:
-        """Column-parallel call above 32 tokens: the shard's tcgen05 GEMM stores its result as tagged bf16x2 words
-        into every rank's exchange buffer (its columns of the [m][n/2] word grid), then the receive kernel
-        assembles [m, n] from this rank's buffer (the same words, epochs and parity halves as the GEMV calls)."""
+        """A call above 32 tokens through the tcgen05 GEMM's peer stores.  Column-parallel: the shard's result as
+        tagged bf16x2 words into every rank's buffer (its columns of the [m][n/2] word grid), assembled by the
+        receive kernel.  Row-parallel (2 ranks): the shard's FP32 partial of all n outputs as tagged f32 words
+        into slot `rank` of every rank's buffer, summed in rank order and rounded by the receive kernel.  Same
+        words, epochs and parity halves as the GEMV calls."""
         p = self.plan
         m = x.shape[0]
         out = torch.empty((m, p.n), dtype=torch.bfloat16, device=x.device)
-        ns = p.n // p.world
         sync = self._sync
-        check(lib().mbp_gemm_c12_multi(ctypes.byref(self.packed.desc), ctypes.c_void_p(x.data_ptr()), m, ns,
-                                       self._xbuf.local_first(p.rank * (ns // 2) * 8), p.world, p.n // 2,
-                                       OUT_TAGGED_BF16X2, ctypes.c_void_p(sync.counter.data_ptr()), self._par,
-                                       _stream()), "mbp_gemm_c12_multi")
-        sync.finish(self._xbuf, self._par, TP_GATHER_BF16, m, p.n, out)
+        epoch = ctypes.c_void_p(sync.counter.data_ptr())
+        if p.mode == "column":
+            ns = p.n // p.world
+            check(lib().mbp_gemm_c12_multi(ctypes.byref(self.packed.desc), ctypes.c_void_p(x.data_ptr()), m, ns,
+                                           self._xbuf.local_first(p.rank * (ns // 2) * 8), p.world, p.n // 2,
+                                           OUT_TAGGED_BF16X2, epoch, self._par, _stream()), "mbp_gemm_c12_multi")
+            sync.finish(self._xbuf, self._par, TP_GATHER_BF16, m, p.n, out)
+            return out
+        xs = p.x_slice(x)  # this rank's K columns, contiguous for the GEMM's x tiles
+        check(lib().mbp_gemm_c12_multi(ctypes.byref(self.packed.desc), ctypes.c_void_p(xs.data_ptr()), m, p.n,
+                                       self._xbuf.local_first(p.rank * m * p.n * 8), p.world, p.n,
+                                       OUT_TAGGED_F32, epoch, self._par, _stream()), "mbp_gemm_c12_multi")
+        sync.finish(self._xbuf, self._par, TP_SUM_F32, m, p.n, out)
         return out
 
     def _local(self, x: torch.Tensor, out_dtype) -> torch.Tensor:
@@ -359,7 +376,8 @@ class TPLinear:
             raise RuntimeError("TPLinear used after close()")
         p = self.plan
         m = x.shape[0]
-        if (self._xbuf is not None and p.mode == "column" and GEMV_MAX_M < m <= GEMM_EXCHANGE_MAX_M):
+        if (self._xbuf is not None and GEMV_MAX_M < m <= GEMM_EXCHANGE_MAX_M
+                and (p.mode == "column" or (self.reduce == "all" and self._gemm_row_p2p()))):
             if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != p.k or not x.is_contiguous():
                 raise ValueError(f"x must be a contiguous bf16 [m, {p.k}] tensor")
             if x.device != self.packed.units.device:

@@ -188,30 +188,34 @@ def test_gemm_decode_shapes(layer, m, variant):
     assert_reference_norms(out, ref)
 
 
+@pytest.mark.parametrize("kind", ["gather", "sum"])
 @pytest.mark.parametrize("n,k,m", [(2048, 1024, 100), (1536, 6144, 256), (1024, 2048, 48)])
-def test_gemm_tagged_exchange_single_rank(n, k, m):
-    """The GEMM's tensor-parallel column-gather epilogue (mbp_gemm_c12_multi: epoch-tagged bf16x2 words into the
-    exchange buffers) read back by the receive kernel (mbp_tp_finish, MBP_TP_GATHER_BF16) with one rank: the
-    assembled output equals the plain GEMM bit for bit over three epochs (alternating buffer halves), with and
-    without a K split."""
+def test_gemm_tagged_exchange_single_rank(n, k, m, kind):
+    """The GEMM's tensor-parallel epilogues (mbp_gemm_c12_multi: epoch-tagged bf16x2 words for the column gather,
+    f32 words for the row-parallel sum, into the exchange buffers) read back by the receive kernel (mbp_tp_finish,
+    MBP_TP_GATHER_BF16 / MBP_TP_SUM_F32) with one rank: the assembled output equals the plain GEMM bit for bit
+    over three epochs (alternating buffer halves), with and without a K split."""
     import ctypes
     import mbp
-    from mbp._lib import OUT_TAGGED_BF16X2, TP_COUNTER_SLOTS, TP_GATHER_BF16, lib
+    from mbp._lib import OUT_TAGGED_BF16X2, OUT_TAGGED_F32, TP_COUNTER_SLOTS, TP_GATHER_BF16, TP_SUM_F32, lib
     from mbp.ops import _stream
     w = weight(n, k, seed=3, escape_frac=0.01)
     p = mbp.pack_c12(w)
-    par = -(-(m * (n // 2) * 8) // 256) * 256
+    gather = kind == "gather"
+    ldo = n // 2 if gather else n
+    par = -(-(m * ldo * 8) // 256) * 256
     buf = torch.zeros(2 * par, dtype=torch.uint8, device="cuda")
     counter = torch.zeros(TP_COUNTER_SLOTS + 1, dtype=torch.int32, device="cuda")
     outs = (ctypes.c_void_p * 1)(buf.data_ptr())
     for i in range(3):
         x = tokens(m, k, seed=10 + i)
         out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
-        rc = lib().mbp_gemm_c12_multi(ctypes.byref(p.desc), x.data_ptr(), m, n, outs, 1, n // 2, OUT_TAGGED_BF16X2,
-                                      counter.data_ptr(), par, _stream())
+        rc = lib().mbp_gemm_c12_multi(ctypes.byref(p.desc), x.data_ptr(), m, n, outs, 1, ldo,
+                                      OUT_TAGGED_BF16X2 if gather else OUT_TAGGED_F32, counter.data_ptr(), par,
+                                      _stream())
         assert rc == 0, rc
-        rc = lib().mbp_tp_finish(None, 0, 1, counter.data_ptr(), buf.data_ptr(), par, TP_GATHER_BF16, m, n,
-                                 out.data_ptr(), _stream())
+        rc = lib().mbp_tp_finish(None, 0, 1, counter.data_ptr(), buf.data_ptr(), par,
+                                 TP_GATHER_BF16 if gather else TP_SUM_F32, m, n, out.data_ptr(), _stream())
         assert rc == 0, rc
         assert torch.equal(out, mbp.gemm(p, x)), i
     assert int(counter[0]) == 3
