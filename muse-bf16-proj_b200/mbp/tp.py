@@ -217,6 +217,19 @@ class TPPlan:
         return self.rank * s, (self.rank + 1) * s
 
 
+def exchange_route(mode: str, reduce: str, world: int, m: int, peer_buffers: bool) -> str:
+    """How a call of `m` tokens exchanges: "gemv-p2p" (the GEMV's tagged peer stores, m <= 32), "gemm-p2p" (the
+    tcgen05 GEMM's tagged peer stores: column-parallel up to 256 tokens, row-parallel ones at 2 ranks) or "nccl"
+    (everything else, and every call of a layer without peer buffers)."""
+    if not peer_buffers or m < 1:
+        return "nccl"
+    if m <= GEMV_MAX_M:
+        return "gemv-p2p" if mode == "column" or reduce == "all" else "nccl"
+    if m <= GEMM_EXCHANGE_MAX_M and (mode == "column" or (reduce == "all" and world == 2)):
+        return "gemm-p2p"
+    return "nccl"
+
+
 def row_exchange_for(world: int, requested: str = "auto") -> str:
     """The fused row-parallel exchange a layer of `world` ranks uses: "sum" (every rank's FP32 partial to every
     rank) or "rsag" (reduce-scatter to each tile's owner + BF16 gather); "auto" = "rsag" from 4 ranks on."""
@@ -328,9 +341,9 @@ class TPLinear:
         return out
 
     def _gemm_row_p2p(self) -> bool:
-        """Row-parallel GEMM calls exchange their FP32 partials by peer stores at 2 ranks only: every rank sends
-        its whole [m][n] partial to every rank, (P-1) x 8 m n bytes, which beats NCCL's all-reduce at P = 2 but not
-        beyond (at 256 tokens and P = 8, 88 MB per rank)."""
+        """Row-parallel GEMM calls exchange their FP32 partials by peer stores at 2 ranks only (`exchange_route`):
+        every rank sends its whole [m][n] partial to every rank, (P-1) x 8 m n bytes, which beats NCCL's
+        all-reduce at P = 2 but not beyond (at 256 tokens and P = 8, 88 MB per rank)."""
         return self.plan.mode == "row" and self.plan.world == 2
 
     def _forward_gemm_p2p(self, x: torch.Tensor) -> torch.Tensor:
@@ -375,20 +388,13 @@ class TPLinear:
         if self.packed is None:
             raise RuntimeError("TPLinear used after close()")
         p = self.plan
-        m = x.shape[0]
-        if (self._xbuf is not None and GEMV_MAX_M < m <= GEMM_EXCHANGE_MAX_M
-                and (p.mode == "column" or (self.reduce == "all" and self._gemm_row_p2p()))):
+        route = exchange_route(p.mode, self.reduce, p.world, x.shape[0], self._xbuf is not None)
+        if route != "nccl":
             if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != p.k or not x.is_contiguous():
                 raise ValueError(f"x must be a contiguous bf16 [m, {p.k}] tensor")
             if x.device != self.packed.units.device:
                 raise ValueError("x is not on this rank's device")
-            return self._forward_gemm_p2p(x)
-        if self._xbuf is not None and 1 <= m <= GEMV_MAX_M and (p.mode == "column" or self.reduce == "all"):
-            if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != p.k or not x.is_contiguous():
-                raise ValueError(f"x must be a contiguous bf16 [m, {p.k}] tensor")
-            if x.device != self.packed.units.device:
-                raise ValueError("x is not on this rank's device")
-            return self._forward_p2p(x)
+            return self._forward_gemm_p2p(x) if route == "gemm-p2p" else self._forward_p2p(x)
         if p.mode == "column":
             local = self._local(x, torch.bfloat16)                        # [m, n/P]
             if p.world == 1:

@@ -170,3 +170,14 @@ def test_row_exchange_choice():
     assert row_exchange_for(8, "sum") == "sum" and row_exchange_for(2, "rsag") == "rsag"
     with pytest.raises(ValueError):
         row_exchange_for(4, "ring")
+
+
+def test_exchange_route():
+    """Which exchange each call takes (the GPU paths themselves are checked by tests/tp_worker.py)."""
+    from mbp.tp import exchange_route as r
+    assert r("column", "all", 4, 1, True) == "gemv-p2p" and r("row", "all", 8, 32, True) == "gemv-p2p"
+    assert r("row", "scatter", 2, 8, True) == "nccl"
+    assert r("column", "all", 8, 33, True) == "gemm-p2p" and r("column", "all", 8, 256, True) == "gemm-p2p"
+    assert r("column", "all", 8, 257, True) == "nccl"
+    assert r("row", "all", 2, 256, True) == "gemm-p2p" and r("row", "all", 4, 256, True) == "nccl"
+    assert r("column", "all", 2, 8, False) == "nccl"
