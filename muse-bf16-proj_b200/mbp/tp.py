@@ -388,7 +388,8 @@ class TPLinear:
         if self.packed is None:
             raise RuntimeError("TPLinear used after close()")
         p = self.plan
-        route = exchange_route(p.mode, self.reduce, p.world, x.shape[0], self._xbuf is not None)
+        m = x.shape[0]
+        route = exchange_route(p.mode, self.reduce, p.world, m, self._xbuf is not None)
         if route != "nccl":
             if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != p.k or not x.is_contiguous():
                 raise ValueError(f"x must be a contiguous bf16 [m, {p.k}] tensor")
@@ -402,10 +403,7 @@ class TPLinear:
             ns = p.n // p.world
             gathered = torch.empty((p.world * m, ns), dtype=torch.bfloat16, device=x.device)
             dist.all_gather_into_tensor(gathered, local, group=self.group)  # [P][m][ns]
-            out = torch.empty((m, p.n), dtype=torch.bfloat16, device=x.device)
-            check(lib().mbp_tp_assemble_columns(ctypes.c_void_p(gathered.data_ptr()), ctypes.c_void_p(out.data_ptr()),
-                                                p.world, m, ns, _stream()), "mbp_tp_assemble_columns")
-            return out
+            return self._assemble(gathered, m, ns)
         part = self._local(x, torch.float32)                                # [m, n] FP32 partial sums
         if p.world > 1 and self.reduce == "all":
             dist.all_reduce(part, group=self.group)
@@ -416,7 +414,18 @@ class TPLinear:
             mine = torch.empty((ns, m), dtype=torch.float32, device=x.device)
             dist.reduce_scatter_tensor(mine, part_t, group=self.group)
             part = mine.t().contiguous()                                    # [m, n/P]
-        out = torch.empty(part.shape, dtype=torch.bfloat16, device=x.device)
+        return self._to_bf16(part)
+
+    def _assemble(self, gathered: torch.Tensor, m: int, ns: int) -> torch.Tensor:
+        """[P][m][ns] gathered shard outputs -> [m, n] (the NCCL column path's assembly kernel)."""
+        out = torch.empty((m, self.plan.n), dtype=torch.bfloat16, device=gathered.device)
+        check(lib().mbp_tp_assemble_columns(ctypes.c_void_p(gathered.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                            self.plan.world, m, ns, _stream()), "mbp_tp_assemble_columns")
+        return out
+
+    def _to_bf16(self, part: torch.Tensor) -> torch.Tensor:
+        """Summed FP32 partials -> BF16 (the NCCL row path's rounding kernel)."""
+        out = torch.empty(part.shape, dtype=torch.bfloat16, device=part.device)
         check(lib().mbp_f32_to_bf16(ctypes.c_void_p(part.data_ptr()), ctypes.c_void_p(out.data_ptr()), part.numel(),
                                     _stream()), "mbp_f32_to_bf16")
         return out

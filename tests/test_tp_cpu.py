@@ -181,3 +181,58 @@ def test_exchange_route():
     assert r("column", "all", 8, 257, True) == "nccl"
     assert r("row", "all", 2, 256, True) == "gemm-p2p" and r("row", "all", 4, 256, True) == "nccl"
     assert r("column", "all", 2, 8, False) == "nccl"
+
+
+def _worker_forward(rank, world, port, errq):
+    """TPLinear.forward's collective path on gloo ranks: routing, the collectives and the shapes around them, with
+    the device kernels (shard GEMV/GEMM, assembly, BF16 rounding) replaced by CPU equivalents of the oracle."""
+    try:
+        _setup(rank, world, port)
+        from types import SimpleNamespace
+        from mbp.tp import TPLinear, TPPlan
+        from oracle import oracle
+        g = torch.Generator().manual_seed(0)
+        n, k = 128, 256
+        w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+        for mode, reduce in (("column", "all"), ("row", "all")):
+            lin = object.__new__(TPLinear)
+            lin.plan = TPPlan(mode, world, rank, n, k)
+            lin.reduce, lin.group, lin._xbuf = reduce, None, None
+            lin.packed = SimpleNamespace(units=torch.empty(0))
+            pk = oracle.pack(_bits(lin.plan.shard(w)), tile_base=True)
+
+            def local(x, dt, pk=pk, lin=lin):
+                out, _ = oracle.gemv_packed(_bits(lin.plan.x_slice(x)), pk)
+                return torch.from_numpy(out).to(dt)
+
+            lin._local = local
+            lin._assemble = lambda gathered, m, ns, lin=lin: (
+                gathered.view(world, m, ns).permute(1, 0, 2).reshape(m, lin.plan.n))
+            lin._to_bf16 = lambda part: part.to(torch.bfloat16)
+            for m in (1, 40, 300):  # the GEMV, GEMM and beyond-exchange sizes all take the collective path here
+                x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+                full = torch.from_numpy(oracle.linear_f64(_bits(x), _bits(w))).float()
+                out = lin.forward(x)
+                assert out.shape == (m, n) and out.dtype == torch.bfloat16, (mode, m, out.shape)
+                assert torch.allclose(out.float(), full, rtol=1e-2, atol=1e-2), (mode, m)
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+def test_tp_forward_collective_path_gloo():
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    errq = ctx.Queue()
+    procs = [ctx.Process(target=_worker_forward, args=(r, world, port, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert all(p.exitcode == 0 for p in procs), errs
