@@ -1,5 +1,8 @@
 // Verify-path GEMM for larger token counts (M > 32): out[m, n] = x[m, k] . W[n, k]^T on the 5th-generation
-// tensor cores (tcgen05 + TMEM), weights unpacked from the 12-bit format in shared memory.
+// tensor cores (tcgen05 + TMEM), weights decoded from the 12-bit format in registers and written into TMEM.
+// The same kernel runs the FP32 router above 256 tokens (hi/lo units, k_gemm<true>) and, for tensor-parallel
+// calls, can store its results as epoch-tagged words into the ranks' exchange buffers (peer pointers) instead of
+// `out` (mbp_gemm_c12_multi).
 //
 // Replaces the reference's dense BF16 verify GEMMs (submission.py: ss_gemm S:783<17-123>, q_kernel
 // S:979<25-170>, qb_kernel S:4576, ol_projection S:1547<18-106>, projection S:2985) and its cuBLASLt routes
